@@ -1,0 +1,374 @@
+"""Benchmark of the B200 attention forward (one JSON line on rank 0).
+
+Metric: attention TFLOP/s, algorithmic FLOPs = 4*Sq*Sk*d per
+(batch, head) slice, halved when causal, as a fraction of the dense TF32
+roofline.  A step is one forward over one batch of the workload with its
+inputs resident in HBM.  Default workload
+(32 heads x 4096 x 128, causal, N(0,1)*0.5 from seed 1), f32 inputs,
+TF32 tensor-core arithmetic.  Inputs (268 MB) are larger than the 126 MB L2, so
+no flush is needed between steps.
+
+Multi-GPU: launched by torchrun, one process per GPU over NCCL.  The (batch,
+head) slices are independent, so every rank runs its own full config-2 batch
+(weak scaling) with no data-path collective; the barrier and the max-over-ranks
+of the CUDA-event times are the only communication.
+
+`--impl reference` times the CPU implementation of the same path (the C
+restatement of the crate's v2 forward; the crate itself cannot be built here)
+on the host cores, on a bounded sample of the workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "flash-attention-cpu_b200"))
+sys.path.insert(0, os.path.join(ROOT, "tests"))
+
+CONFIGS = {
+    # name: (bh, sq, sk, d, causal, seed, factor, description)
+    "c1": (1, 512, 512, 64, False, 0, 1.0, "1 head x 512 x 64, non-causal"),
+    "c2": (32, 4096, 4096, 128, True, 1, 0.5, "32 heads x 4096 x 128, causal prefill"),
+    "c3": (256, 1024, 1024, 64, False, 2, 1.0, "16 batch x 16 heads x 1024 x 64, non-causal"),
+    "c4": (64, 1, 32768, 128, False, 3, 1.0, "64 heads, Sq=1, Sk=32768, d128 decode"),
+    "c5": (1, 131072, 131072, 128, True, 4, 0.3, "1 head x 131072 x 128, causal"),
+}
+PRECISION_NAMES = {"tf32": 0, "3xtf32": 1, "fp32": 2}
+
+
+def flops_of(bh, sq, sk, d, causal):
+    """Algorithmic FLOPs: 4*Sq*Sk*d per slice, halved when causal."""
+    f = 4.0 * sq * sk * d * bh
+    return f / 2 if causal else f
+
+
+def bytes_of(bh, sq, sk, d):
+    """Algorithmic bytes: one read of Q, K, V and one write of O (f32)."""
+    return 4.0 * bh * (2 * sq * d + 2 * sk * d)
+
+
+def measured_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return json.load(f)
+    except OSError:
+        return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms."""
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        rows = []
+        try:
+            with open(self.path) as f:
+                for line in f:
+                    parts = [p.strip() for p in line.split(",")]
+                    if len(parts) >= 9:
+                        rows.append(parts)
+        except OSError:
+            pass
+        finally:
+            if self.path:
+                os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i] == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(rows)}
+
+
+def cpu_baseline(cfg, budget_s=12.0):
+    """Times the oracle (the crate's v2 forward restated in C, all host cores) on
+    whole heads of the workload, as many as fit in ~budget_s.  Returns a dict."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import numpy as np
+    import oracle as O
+    bh, sq, sk, d, causal, seed, factor, _ = cfg
+    cores = os.cpu_count() or 1
+    rng = np.random.default_rng(seed)
+
+    def sample(nh):
+        q = rng.standard_normal(nh * sq * d, dtype=np.float32) * np.float32(factor)
+        k = rng.standard_normal(nh * sk * d, dtype=np.float32) * np.float32(factor)
+        v = rng.standard_normal(nh * sk * d, dtype=np.float32) * np.float32(factor)
+        return q, k, v
+
+    # C5 is one 4.4-TFLOP head: sample its query blocks instead of whole heads.
+    if bh == 1 and sq * sk > 1 << 32:
+        q, k, v = sample(1)
+        n_items = (sq + 63) // 64
+        take = max(cores, 64)
+        t0 = time.perf_counter()
+        O.flash_v2_multihead(q, k, v, 1, sq, sk, d, causal, nthreads=cores, max_items=take)
+        dt = time.perf_counter() - t0
+        # FLOPs of the first `take` 64-row blocks
+        rows = range(min(sq, take * 64))
+        fl = 4.0 * d * sum((min(sk, r + 1) if causal else sk) for r in rows)
+        return {"value": fl / dt / 1e12, "unit": "TFLOP/s", "cores": cores, "kind": "port",
+                "sample": f"first {take} of {n_items} 64-row query blocks of the head "
+                          f"({fl / 1e9:.1f} GFLOP) in {dt:.2f} s",
+                "tier": O.tier()}
+    q, k, v = sample(1)
+    t0 = time.perf_counter()
+    O.flash_v2_multihead(q, k, v, 1, sq, sk, d, causal, nthreads=cores)
+    dt1 = time.perf_counter() - t0
+    nh = int(max(1, min(bh, budget_s / max(dt1, 1e-6))))
+    q, k, v = sample(nh)
+    t0 = time.perf_counter()
+    O.flash_v2_multihead(q, k, v, nh, sq, sk, d, causal, nthreads=cores)
+    dt = time.perf_counter() - t0
+    fl = flops_of(nh, sq, sk, d, causal)
+    return {"value": fl / dt / 1e12, "unit": "TFLOP/s", "cores": cores, "kind": "port",
+            "sample": f"{nh} of {bh} slices ({fl / 1e9:.1f} GFLOP) in {dt:.2f} s",
+            "tier": O.tier()}
+
+
+def dist_setup(n_gpus):
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return rank, world, local
+
+
+def run_reference(args):
+    """--impl reference: the CPU implementation of the path, rank 0 only."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    cfg = CONFIGS[args.config]
+    bh, sq, sk, d, causal = cfg[:5]
+    vals = []
+    base = None
+    for i in range(args.warmup + args.steps):
+        b = cpu_baseline(cfg, budget_s=args.ref_budget)
+        if i >= args.warmup:
+            vals.append(b["value"])
+            base = b
+    value = statistics.median(vals)
+    base["value"] = value
+    line = {"metric": "attention TFLOP/s", "impl": "reference", "value": value,
+            "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": None, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": config_dict(args, cfg, world=1),
+            "cpu_baseline": base,
+            "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def config_dict(args, cfg, world):
+    bh, sq, sk, d, causal, seed, factor, desc = cfg
+    return {"workload": f"{args.config}: {desc}", "batch_heads_per_gpu": bh, "seq_len_q": sq,
+            "seq_len_k": sk, "d_head": d, "causal": causal, "seed": seed,
+            "input_scale": factor, "precision": args.precision,
+            "parallelism": f"dp{world} ((batch, head) slices per GPU, no collective)",
+            "l2": "inputs larger than L2 (no flush)" if bytes_of(bh, sq, sk, d) > 126e6
+            else "L2 flushed between steps (256 MB write)"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--config", default="c2", choices=sorted(CONFIGS))
+    ap.add_argument("--precision", default="tf32", choices=sorted(PRECISION_NAMES))
+    ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ref-budget", type=float, default=8.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args)
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    import fa_b200
+
+    rank, world, local = dist_setup(args.gpus)
+    fa_b200.set_device(torch.cuda.current_device())
+    fa_b200.set_precision(PRECISION_NAMES[args.precision])
+    cfg = CONFIGS[args.config]
+    bh, sq, sk, d, causal, seed, factor, _ = cfg
+    dev = torch.device("cuda", torch.cuda.current_device())
+
+    # inputs of this rank's slices: the config's generator, offset per rank
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(seed * 1000 + rank)
+    q = torch.randn(bh, sq, d, device=dev, generator=gen) * factor
+    k = torch.randn(bh, sk, d, device=dev, generator=gen) * factor
+    v = torch.randn(bh, sk, d, device=dev, generator=gen) * factor
+    out = torch.empty_like(q)
+    lse = torch.empty(bh, sq, device=dev)
+    flush = None
+    if bytes_of(bh, sq, sk, d) <= 126e6:
+        flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream()
+
+    def step():
+        if flush is not None:
+            flush.fill_(1.0)
+        fa_b200.forward_device(q, k, v, out, lse, causal=causal, stream=stream)
+
+    for _ in range(args.warmup):
+        step()
+    fa_b200.sync_status(stream)
+
+    # device-timed region: every launch of the step on `stream`
+    kernel_ms = []
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    launches0 = fa_b200.launch_count()
+    with ClockSampler(local) as clk:
+        t_start = torch.cuda.Event(enable_timing=True)
+        t_end = torch.cuda.Event(enable_timing=True)
+        t_start.record(stream)
+        for i in range(args.steps):
+            if flush is not None:
+                flush.fill_(1.0)
+            ev[i][0].record(stream)
+            fa_b200.forward_device(q, k, v, out, lse, causal=causal, stream=stream)
+            ev[i][1].record(stream)
+        t_end.record(stream)
+        torch.cuda.synchronize()
+    launches = fa_b200.launch_count() - launches0
+    fa_b200.sync_status(stream)
+    path = fa_b200.last_path()
+    kernel_ms = [a.elapsed_time(b) for a, b in ev]
+    total_ms = t_start.elapsed_time(t_end)
+    step_ms = sum(kernel_ms) / len(kernel_ms) if flush is not None else total_ms / args.steps
+    t = torch.tensor([step_ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.barrier()
+    step_ms = float(t.item())
+    fl = flops_of(bh, sq, sk, d, causal)
+    value = world * fl / (step_ms * 1e-3) / 1e12
+    clocks = clk.summary()
+
+    # end-to-end through the public host-slice API (pinned host buffers,
+    # H2D of Q/K/V and D2H of OUT inside the timed region, every step)
+    hq = torch.empty(bh * sq * d, dtype=torch.float32, pin_memory=True)
+    hk = torch.empty(bh * sk * d, dtype=torch.float32, pin_memory=True)
+    hv = torch.empty(bh * sk * d, dtype=torch.float32, pin_memory=True)
+    ho = torch.empty(bh * sq * d, dtype=torch.float32, pin_memory=True)
+    hq.copy_(q.view(-1))
+    hk.copy_(k.view(-1))
+    hv.copy_(v.view(-1))
+    nq, nk, nv, no = hq.numpy(), hk.numpy(), hv.numpy(), ho.numpy()
+    cfgc = fa_b200.FlashAttentionConfig(64, 128, causal)
+    fa_b200.flash_attention_multihead_v2(nq, nk, nv, 1, bh, sq, sk, d, cfgc, no)
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.e2e_steps):
+        fa_b200.flash_attention_multihead_v2(nq, nk, nv, 1, bh, sq, sk, d, cfgc, no)
+    e2e_s = (time.perf_counter() - t0) / args.e2e_steps
+    te = torch.tensor([e2e_s], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_s = float(te.item())
+    e2e = {"value": world * fl / e2e_s / 1e12, "unit": "TFLOP/s",
+           "h2d_bytes_per_step": 4 * (bh * sq * d + 2 * bh * sk * d),
+           "d2h_bytes_per_step": 4 * bh * sq * d, "ms_per_step": e2e_s * 1e3,
+           "api": "fa_flash_attention_multihead_v2 (host slices, synchronous)"}
+
+    if rank != 0:
+        if world > 1:
+            dist.destroy_process_group()
+        return
+
+    peaks = measured_peaks()
+    if path.startswith("decode"):
+        bound, unit = "hbm", "GB/s"
+        achieved = bytes_of(bh, sq, sk, d) / (step_ms * 1e-3) / 1e9
+        peak = peaks["hbm_gbs"] if peaks else 6650.0
+        peak_src = "measured hbm_gbs" if peaks else "fallback 6.65 TB/s"
+    else:
+        bound, unit = "tensor", "TFLOP/s"
+        achieved = fl / (step_ms * 1e-3) / 1e12
+        peak = peaks["bf16_tflops"] / 2 if peaks else 1590.0 / 2
+        peak_src = ("dense TF32 = measured bf16 burst / 2" if peaks
+                    else "dense TF32 = fallback bf16 1.59 PF/s / 2")
+    traffic = None
+    try:
+        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+            tr = json.load(f).get(f"{args.config}/{args.precision}")
+            if tr:
+                traffic = tr["bytes_per_launch"]
+    except OSError:
+        pass
+    roof = {"bound": bound, "achieved": achieved, "peak": peak, "unit": unit,
+            "frac": achieved / peak, "traffic": traffic, "peak_source": peak_src,
+            "kernel": path, "launches_per_step": launches / args.steps}
+    line = {"metric": "attention TFLOP/s", "value": value, "unit": "TFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "tf32" if args.precision == "tf32" and not path.startswith(("decode", "simt"))
+            else ("3xtf32" if args.precision == "3xtf32" and path.startswith("tcgen05") else "f32"),
+            "data": "synthetic", "config": config_dict(args, cfg, world),
+            "clocks": clocks, "e2e": e2e, "gpu_launches": launches, "roofline": roof}
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(cfg)
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,427 @@
+// The C ABI (include/fa_b200.h): argument and shape validation with the
+// crate's semantics, host<->device staging for the host-slice calls, kernel
+// selection, and the error side channel.  Every compute step is a kernel of
+// this library; there is no CPU path.
+#include "fa_common.cuh"
+#include "../../include/fa_b200.h"
+
+#include <atomic>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+namespace fa {
+namespace {
+std::atomic<unsigned long long> g_launches{0};
+}
+void count_launch(int n) { g_launches.fetch_add((unsigned long long)n); }
+unsigned long long launches_issued() { return g_launches.load(); }
+}  // namespace fa
+
+namespace {
+
+thread_local std::string t_err;
+thread_local const char* t_path = "";
+
+std::atomic<int> g_precision{-1};
+std::atomic<int> g_device{-1};
+
+constexpr int kMaxDevices = 64;
+struct DeviceState {
+  std::once_flag once;
+  cudaError_t init_err = cudaSuccess;
+  int* err_flag = nullptr;  // device word written by kernels on a bounded-wait timeout
+  int num_sms = 148;
+  int cc_major = 0, cc_minor = 0;
+};
+DeviceState g_dev[kMaxDevices];
+
+int set_err(int code, const std::string& msg) {
+  t_err = msg;
+  return code;
+}
+int cuda_err(cudaError_t e, const char* what) {
+  return set_err(FA_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+int env_precision() {
+  const char* s = std::getenv("FA_B200_PRECISION");
+  if (!s) return FA_PREC_3XTF32;
+  if (!strcmp(s, "tf32") || !strcmp(s, "TF32")) return FA_PREC_TF32;
+  if (!strcmp(s, "fp32") || !strcmp(s, "FP32")) return FA_PREC_FP32;
+  return FA_PREC_3XTF32;
+}
+int precision() {
+  int p = g_precision.load();
+  if (p < 0) {
+    int e = env_precision();
+    g_precision.compare_exchange_strong(p, e);
+    p = g_precision.load();
+  }
+  return p;
+}
+
+// Make the library's device current and initialise its state once.
+int prepare_device(int* dev_out) {
+  int n = 0;
+  cudaError_t e = cudaGetDeviceCount(&n);
+  if (e != cudaSuccess || n == 0) {
+    cudaGetLastError();
+    return set_err(FA_ERR_NO_DEVICE, "no CUDA device available (this library has no CPU path)");
+  }
+  int dev = g_device.load();
+  if (dev < 0) {
+    e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_err(e, "cudaGetDevice");
+  } else {
+    e = cudaSetDevice(dev);
+    if (e != cudaSuccess) return cuda_err(e, "cudaSetDevice");
+  }
+  if (dev >= kMaxDevices) return set_err(FA_ERR_ARG, "device index too large");
+  DeviceState& st = g_dev[dev];
+  std::call_once(st.once, [&] {
+    cudaDeviceProp prop;
+    st.init_err = cudaGetDeviceProperties(&prop, dev);
+    if (st.init_err != cudaSuccess) return;
+    st.num_sms = prop.multiProcessorCount;
+    st.cc_major = prop.major;
+    st.cc_minor = prop.minor;
+    st.init_err = cudaMalloc(&st.err_flag, sizeof(int));
+    if (st.init_err != cudaSuccess) return;
+    st.init_err = cudaMemset(st.err_flag, 0, sizeof(int));
+    if (st.init_err != cudaSuccess) return;
+    // Keep freed stream-ordered allocations cached in the pool.
+    cudaMemPool_t pool;
+    if (cudaDeviceGetDefaultMemPool(&pool, dev) == cudaSuccess) {
+      uint64_t thr = ~0ull;
+      cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &thr);
+    }
+  });
+  if (st.init_err != cudaSuccess) return cuda_err(st.init_err, "device initialisation");
+  if (st.cc_major != 10)
+    return set_err(FA_ERR_NO_DEVICE, "this library is built for sm_100a (B200) only");
+  *dev_out = dev;
+  return FA_OK;
+}
+
+bool mul_ok(size_t a, size_t b, size_t* r) {
+  if (a != 0 && b > SIZE_MAX / a) return false;
+  *r = a * b;
+  return true;
+}
+
+// Kernel selection for one forward over bh slices.
+int dispatch(fa::FwdParams p, int dev, cudaStream_t s) {
+  const int prec = precision();
+  DeviceState& st = g_dev[dev];
+  p.err = st.err_flag;
+  p.scale = 1.0f / sqrtf((float)p.d);
+  p.scale_log2 = p.scale * 1.4426950408889634f;
+  cudaError_t e = cudaSuccess;
+  if (p.sq <= 16 && fa::decode_supported(p.d)) {
+    // Few query rows: split the key range so every SM streams K/V.
+    t_path = "decode_splitkv";
+    const int splits = fa::decode_pick_splits(p.bh, p.sq, p.sk, st.num_sms);
+    float* scratch = nullptr;
+    if (splits > 1) {
+      size_t n = (size_t)splits * p.bh * p.sq * (p.d + 1);
+      e = cudaMallocAsync((void**)&scratch, n * sizeof(float), s);
+      if (e != cudaSuccess) return cuda_err(e, "cudaMallocAsync(split partials)");
+    }
+    // grid.y holds the slice index: at most 65535 slices per launch.
+    for (int b0 = 0; b0 < p.bh && e == cudaSuccess; b0 += 65535) {
+      fa::FwdParams q = p;
+      q.bh = p.bh - b0 < 65535 ? p.bh - b0 : 65535;
+      q.q += (size_t)b0 * p.sq * p.d;
+      q.k += (size_t)b0 * p.sk * p.d;
+      q.v += (size_t)b0 * p.sk * p.d;
+      q.o += (size_t)b0 * p.sq * p.d;
+      if (q.lse) q.lse += (size_t)b0 * p.sq;
+      e = fa::launch_decode(q, splits, scratch, s);
+    }
+    if (scratch) cudaFreeAsync(scratch, s);
+    if (e != cudaSuccess) return cuda_err(e, "decode launch");
+    return FA_OK;
+  }
+  if (fa::tc_supported(p.d, prec)) {
+    t_path = prec == FA_PREC_TF32 ? "tcgen05_tf32" : "tcgen05_3xtf32";
+    e = fa::launch_tc(p, prec, nullptr, 0, s);
+    if (e != cudaSuccess) return cuda_err(e, "tcgen05 launch");
+    return FA_OK;
+  }
+  if (p.d <= 256) {
+    t_path = "simt_fp32";
+    for (int b0 = 0; b0 < p.bh && e == cudaSuccess; b0 += 65535) {
+      fa::FwdParams q = p;
+      q.bh = p.bh - b0 < 65535 ? p.bh - b0 : 65535;
+      q.q += (size_t)b0 * p.sq * p.d;
+      q.k += (size_t)b0 * p.sk * p.d;
+      q.v += (size_t)b0 * p.sk * p.d;
+      q.o += (size_t)b0 * p.sq * p.d;
+      if (q.lse) q.lse += (size_t)b0 * p.sq;
+      e = fa::launch_simt(q, s);
+    }
+    if (e != cudaSuccess) return cuda_err(e, "simt launch");
+    return FA_OK;
+  }
+  return set_err(FA_ERR_UNSUPPORTED, "d_head > 256 is not supported");
+}
+
+// Reads and clears the device error word after the stream has finished.
+int check_err_flag(int dev, cudaStream_t s) {
+  int h = 0;
+  cudaError_t e = cudaMemcpyAsync(&h, g_dev[dev].err_flag, sizeof(int), cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return cuda_err(e, "kernel execution");
+  if (h != 0) {
+    cudaMemsetAsync(g_dev[dev].err_flag, 0, sizeof(int), s);
+    cudaStreamSynchronize(s);
+    return set_err(FA_ERR_TIMEOUT, "a bounded in-kernel wait expired (kernel aborted)");
+  }
+  return FA_OK;
+}
+
+struct HostCallStream {
+  cudaStream_t s[kMaxDevices] = {};
+  ~HostCallStream() {}
+};
+thread_local HostCallStream t_streams;
+
+int host_stream(int dev, cudaStream_t* out) {
+  if (!t_streams.s[dev]) {
+    cudaError_t e = cudaStreamCreateWithFlags(&t_streams.s[dev], cudaStreamNonBlocking);
+    if (e != cudaSuccess) return cuda_err(e, "cudaStreamCreate");
+  }
+  *out = t_streams.s[dev];
+  return FA_OK;
+}
+
+// Host-slice forward: stage to HBM, run, copy back, check.
+int host_forward(const float* q, const float* k, const float* v, size_t bh, size_t sq,
+                 size_t sk, size_t d, int causal, float* out, float* lse) {
+  if (bh > (size_t)INT32_MAX || sq > (size_t)INT32_MAX || sk > (size_t)INT32_MAX || d > 256)
+    return set_err(d > 256 ? FA_ERR_UNSUPPORTED : FA_ERR_ARG, "dimension too large");
+  int dev = 0;
+  int rc = prepare_device(&dev);
+  if (rc) return rc;
+  cudaStream_t s;
+  if ((rc = host_stream(dev, &s))) return rc;
+  const size_t nq = bh * sq * d, nk = bh * sk * d, nl = bh * sq;
+  const size_t bytes = (2 * nq + 2 * nk + nl) * sizeof(float);
+  char* buf = nullptr;
+  cudaError_t e = cudaMallocAsync((void**)&buf, bytes, s);
+  if (e != cudaSuccess) return cuda_err(e, "cudaMallocAsync(staging)");
+  float* dq = (float*)buf;
+  float* dk = dq + nq;
+  float* dv = dk + nk;
+  float* dout = dv + nk;
+  float* dlse = dout + nq;
+  e = cudaMemcpyAsync(dq, q, nq * sizeof(float), cudaMemcpyHostToDevice, s);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(dk, k, nk * sizeof(float), cudaMemcpyHostToDevice, s);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(dv, v, nk * sizeof(float), cudaMemcpyHostToDevice, s);
+  if (e != cudaSuccess) {
+    cudaFreeAsync(buf, s);
+    return cuda_err(e, "host-to-device copy");
+  }
+  fa::FwdParams p{};
+  p.q = dq; p.k = dk; p.v = dv; p.o = dout; p.lse = lse ? dlse : nullptr;
+  p.bh = (int)bh; p.sq = (int)sq; p.sk = (int)sk; p.d = (int)d;
+  p.q_offset = 0; p.k_offset = 0; p.causal = causal ? 1 : 0;
+  rc = dispatch(p, dev, s);
+  if (rc == FA_OK) rc = check_err_flag(dev, s);
+  if (rc == FA_OK) {
+    e = cudaMemcpyAsync(out, dout, nq * sizeof(float), cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess && lse)
+      e = cudaMemcpyAsync(lse, dlse, nl * sizeof(float), cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) rc = cuda_err(e, "device-to-host copy");
+  }
+  cudaFreeAsync(buf, s);
+  cudaStreamSynchronize(s);
+  return rc;
+}
+
+int single_head(const float* q, size_t q_len, const float* k, size_t k_len, const float* v,
+                size_t v_len, size_t sq, size_t sk, size_t d, const fa_config* cfg, float* out,
+                size_t out_len) {
+  t_err.clear();
+  size_t nq, nk;
+  if (!mul_ok(sq, d, &nq) || !mul_ok(sk, d, &nk)) return set_err(FA_ERR_ARG, "size overflow");
+  // Same order and messages as src/common.rs:51-54.
+  if (q_len != nq) return set_err(FA_ERR_SHAPE, "q shape mismatch");
+  if (k_len != nk) return set_err(FA_ERR_SHAPE, "k shape mismatch");
+  if (v_len != nk) return set_err(FA_ERR_SHAPE, "v shape mismatch");
+  if (out_len != nq) return set_err(FA_ERR_SHAPE, "out shape mismatch");
+  if (sq == 0 || sk == 0 || d == 0) return FA_OK;  // out untouched (common.rs:56)
+  if (!q || !k || !v || !out) return set_err(FA_ERR_ARG, "null buffer pointer");
+  const int causal = cfg ? (cfg->causal != 0) : 0;
+  return host_forward(q, k, v, 1, sq, sk, d, causal, out, nullptr);
+}
+
+int multi_head(const float* q, size_t q_len, const float* k, size_t k_len, const float* v,
+               size_t v_len, size_t batch, size_t heads, size_t sq, size_t sk, size_t d,
+               const fa_config* cfg, float* out, size_t out_len) {
+  t_err.clear();
+  size_t bh, per_q, per_k, nq, nk;
+  if (!mul_ok(batch, heads, &bh) || !mul_ok(sq, d, &per_q) || !mul_ok(sk, d, &per_k) ||
+      !mul_ok(bh, per_q, &nq) || !mul_ok(bh, per_k, &nk))
+    return set_err(FA_ERR_ARG, "size overflow");
+  // src/common.rs:87-90 (the crate's multihead asserts carry no message).
+  if (q_len != nq) return set_err(FA_ERR_SHAPE, "multihead q shape mismatch");
+  if (k_len != nk) return set_err(FA_ERR_SHAPE, "multihead k shape mismatch");
+  if (v_len != nk) return set_err(FA_ERR_SHAPE, "multihead v shape mismatch");
+  if (out_len != nq) return set_err(FA_ERR_SHAPE, "multihead out shape mismatch");
+  if (bh == 0 || sq == 0 || sk == 0 || d == 0) return FA_OK;
+  if (!q || !k || !v || !out) return set_err(FA_ERR_ARG, "null buffer pointer");
+  const int causal = cfg ? (cfg->causal != 0) : 0;
+  return host_forward(q, k, v, bh, sq, sk, d, causal, out, nullptr);
+}
+
+int device_forward(const float* q, const float* k, const float* v, float* out, float* lse,
+                   size_t bh, size_t sq, size_t sk, size_t d, int causal, size_t q_off,
+                   size_t k_off, void* stream) {
+  t_err.clear();
+  if (bh == 0 || sq == 0 || sk == 0 || d == 0) return FA_OK;
+  if (!q || !k || !v || !out) return set_err(FA_ERR_ARG, "null buffer pointer");
+  if (bh > (size_t)INT32_MAX || sq > (size_t)INT32_MAX || sk > (size_t)INT32_MAX)
+    return set_err(FA_ERR_ARG, "dimension too large");
+  if (d > 256) return set_err(FA_ERR_UNSUPPORTED, "d_head > 256 is not supported");
+  int dev = 0;
+  int rc = prepare_device(&dev);
+  if (rc) return rc;
+  fa::FwdParams p{};
+  p.q = q; p.k = k; p.v = v; p.o = out; p.lse = lse;
+  p.bh = (int)bh; p.sq = (int)sq; p.sk = (int)sk; p.d = (int)d;
+  p.q_offset = (long long)q_off; p.k_offset = (long long)k_off;
+  p.causal = causal ? 1 : 0;
+  return dispatch(p, dev, (cudaStream_t)stream);
+}
+
+}  // namespace
+
+extern "C" {
+
+fa_config fa_config_default(void) {
+  fa_config c;
+  c.block_size_q = 64;
+  c.block_size_kv = 128;
+  c.causal = 0;
+  return c;
+}
+
+#define FA_SINGLE(name)                                                                       \
+  int name(const float* q, size_t q_len, const float* k, size_t k_len, const float* v,       \
+           size_t v_len, size_t sq, size_t sk, size_t d, const fa_config* cfg, float* out,    \
+           size_t out_len) {                                                                  \
+    return single_head(q, q_len, k, k_len, v, v_len, sq, sk, d, cfg, out, out_len);           \
+  }
+FA_SINGLE(fa_flash_attention_v1)
+FA_SINGLE(fa_flash_attention_v2)
+FA_SINGLE(fa_flash_attention_v3)
+FA_SINGLE(fa_flash_attention)
+#undef FA_SINGLE
+
+#define FA_MULTI(name)                                                                        \
+  int name(const float* q, size_t q_len, const float* k, size_t k_len, const float* v,       \
+           size_t v_len, size_t batch, size_t heads, size_t sq, size_t sk, size_t d,          \
+           const fa_config* cfg, float* out, size_t out_len) {                                \
+    return multi_head(q, q_len, k, k_len, v, v_len, batch, heads, sq, sk, d, cfg, out,        \
+                      out_len);                                                               \
+  }
+FA_MULTI(fa_flash_attention_multihead_v1)
+FA_MULTI(fa_flash_attention_multihead_v2)
+FA_MULTI(fa_flash_attention_multihead_v3)
+FA_MULTI(fa_flash_attention_multihead)
+#undef FA_MULTI
+
+int fa_flash_attention_multihead_lse(const float* q, const float* k, const float* v,
+                                     size_t batch_heads, size_t sq, size_t sk, size_t d,
+                                     int causal, float* out, float* lse) {
+  t_err.clear();
+  if (batch_heads == 0 || sq == 0 || sk == 0 || d == 0) return FA_OK;
+  if (!q || !k || !v || !out) return set_err(FA_ERR_ARG, "null buffer pointer");
+  return host_forward(q, k, v, batch_heads, sq, sk, d, causal, out, lse);
+}
+
+int fa_forward_device(const float* q, const float* k, const float* v, float* out, float* lse,
+                      size_t bh, size_t sq, size_t sk, size_t d, int causal, void* stream) {
+  return device_forward(q, k, v, out, lse, bh, sq, sk, d, causal, 0, 0, stream);
+}
+
+int fa_forward_partial_device(const float* q, const float* k, const float* v, float* out,
+                              float* lse, size_t bh, size_t sq, size_t sk, size_t d, int causal,
+                              size_t q_offset, size_t k_offset, void* stream) {
+  return device_forward(q, k, v, out, lse, bh, sq, sk, d, causal, q_offset, k_offset, stream);
+}
+
+int fa_lse_combine_device(const float* o_parts, const float* lse_parts, size_t n_parts,
+                          size_t rows, size_t d, float* out, float* lse_out, void* stream) {
+  t_err.clear();
+  if (rows == 0 || d == 0) return FA_OK;
+  if (n_parts == 0 || !o_parts || !lse_parts || !out)
+    return set_err(FA_ERR_ARG, "null buffer pointer or zero parts");
+  if (rows > (size_t)INT32_MAX || n_parts > (size_t)INT32_MAX || d > 4096)
+    return set_err(FA_ERR_ARG, "dimension too large");
+  int dev = 0;
+  int rc = prepare_device(&dev);
+  if (rc) return rc;
+  t_path = "lse_combine";
+  cudaError_t e = fa::launch_combine(o_parts, lse_parts, (int)n_parts, (long long)rows, (int)d,
+                                     out, lse_out, (cudaStream_t)stream);
+  if (e != cudaSuccess) return cuda_err(e, "combine launch");
+  return FA_OK;
+}
+
+int fa_sync_status(void* stream) {
+  t_err.clear();
+  int dev = 0;
+  int rc = prepare_device(&dev);
+  if (rc) return rc;
+  return check_err_flag(dev, (cudaStream_t)stream);
+}
+
+int fa_set_precision(int p) {
+  if (p < FA_PREC_TF32 || p > FA_PREC_FP32) return set_err(FA_ERR_ARG, "unknown precision");
+  g_precision.store(p);
+  return FA_OK;
+}
+int fa_get_precision(void) { return precision(); }
+
+int fa_set_device(int device) {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) {
+    cudaGetLastError();
+    return set_err(FA_ERR_NO_DEVICE, "no CUDA device available");
+  }
+  if (device < 0 || device >= n) return set_err(FA_ERR_ARG, "device index out of range");
+  g_device.store(device);
+  return FA_OK;
+}
+
+int fa_device_count(void) {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return n;
+}
+
+const char* fa_last_error(void) { return t_err.c_str(); }
+uint64_t fa_launch_count(void) { return fa::launches_issued(); }
+const char* fa_last_path(void) { return t_path; }
+
+void fa_shutdown(void) {
+  for (int d = 0; d < kMaxDevices; d++) {
+    if (t_streams.s[d]) {
+      cudaSetDevice(d);
+      cudaStreamSynchronize(t_streams.s[d]);
+      cudaStreamDestroy(t_streams.s[d]);
+      t_streams.s[d] = nullptr;
+    }
+  }
+}
+
+}  // extern "C"

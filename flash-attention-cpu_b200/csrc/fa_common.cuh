@@ -1,0 +1,79 @@
+// Shared definitions of the B200 attention-forward kernels.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace fa {
+
+// One forward launch over `bh` independent (batch, head) slices.
+// Q/OUT slice stride = sq*d elements, K/V slice stride = sk*d, LSE stride = sq.
+// Causal masking compares global positions: query row i sits at q_offset + i,
+// key j at k_offset + j; key visible iff k_offset + j <= q_offset + i.
+struct FwdParams {
+  const float* q;
+  const float* k;
+  const float* v;
+  float* o;    // normalised output, [bh, sq, d]
+  float* lse;  // nullable, [bh, sq], natural log of the scaled-score row sums
+  int bh, sq, sk, d;
+  long long q_offset, k_offset;
+  int causal;
+  float scale;       // 1/sqrt(d), computed in f32 as the crate does (v2.rs:171)
+  float scale_log2;  // scale * log2(e): scores go straight into exp2
+  int* err;          // device error word (0 = ok), see ErrCode
+};
+
+enum ErrCode : int {
+  kErrNone = 0,
+  kErrTimeout = 1,  // a bounded mbarrier wait expired
+};
+
+// Upper bound on any single in-kernel wait.  No legitimate wait in these
+// kernels lasts more than a few milliseconds.
+constexpr unsigned long long kWaitLimitNs = 2000000000ull;
+
+__device__ __forceinline__ unsigned long long globaltimer_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ float warp_max(float x) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, o));
+  return x;
+}
+__device__ __forceinline__ float warp_sum(float x) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+  return x;
+}
+
+// Visible-key count for query global position qg against keys starting at
+// global position kg0 with n keys: keys [kg0, kg0+n) ∩ (-inf, qg].
+__device__ __forceinline__ int causal_limit(long long qg, long long kg0, int n) {
+  long long lim = qg - kg0 + 1;
+  return lim < 0 ? 0 : (lim > n ? n : (int)lim);
+}
+
+}  // namespace fa
+
+// Launchers implemented in the .cu files; return cudaError_t of the launch.
+namespace fa {
+cudaError_t launch_simt(const FwdParams& p, cudaStream_t s);
+// Split-KV decode family: partial buffers are caller-provided scratch of
+// `splits * bh * sq * (d + 1)` floats (ignored when splits == 1).
+int decode_pick_splits(int bh, int sq, int sk, int num_sms);
+cudaError_t launch_decode(const FwdParams& p, int splits, float* scratch, cudaStream_t s);
+cudaError_t launch_combine(const float* o_parts, const float* lse_parts, int n_parts,
+                           long long rows, int d, float* out, float* lse_out,
+                           cudaStream_t s);
+bool decode_supported(int d);
+// tcgen05 family.  tc_supported() says whether a tensor-core kernel exists for d.
+bool tc_supported(int d, int precision);
+cudaError_t launch_tc(const FwdParams& p, int precision, float* scratch,
+                      size_t scratch_floats, cudaStream_t s);
+size_t tc_scratch_floats(const FwdParams& p, int precision);
+unsigned long long launches_issued();
+void count_launch(int n = 1);
+}  // namespace fa

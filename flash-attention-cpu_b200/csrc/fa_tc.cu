@@ -1,0 +1,550 @@
+// Tensor-core attention forward for sm_100a (B200): tcgen05 TF32 MMAs with
+// the accumulators in tensor memory (TMEM), TMA tile loads into 128-byte
+// swizzled shared memory, and warp-specialised roles on an mbarrier pipeline.
+//
+// One CTA computes one 128-row query tile of one (batch, head) slice:
+//   warp 0 (one lane)  TMA producer: Q tile once, then K and V tiles of BK keys
+//                      through an NS-deep ring (separate K and V slots so a K
+//                      slot frees as soon as its QK^T MMA has read it).
+//   warp 1 (one lane)  MMA issuer: S_b = Q K_j^T into TMEM buffer b = j%2, then
+//                      O += P_{j-1} V_{j-1} with P read straight from TMEM
+//                      (the .kind::tf32 "A from TMEM" form).  Issuing S_j
+//                      before PV_{j-1} lets QK^T of the next tile run while the
+//                      softmax warps work on the current one (the mechanism
+//                      behind the crate's v3 software pipelining,
+//                      src/v3.rs:445-483).
+//   warps 4-7          softmax, one query row per thread: tcgen05.ld the score
+//                      row, mask (causal diagonal tiles and keys past seq_len_k,
+//                      src/v2.rs:268-287), running max, exp2, row sum, P written
+//                      back over S in TMEM (src/v2.rs:289-339).  O is rescaled
+//                      in TMEM only when the running max grows by more than
+//                      2^8 (lazy rescaling); O and l share the same stale max,
+//                      so the final out = O / l (src/v2.rs:375-382) is exact.
+// Causal runs never load or multiply key tiles wholly past the tile's last
+// row (src/v2.rs:210-212), and CTAs are dispatched heaviest-tile first.
+//
+// Shared-memory layouts (all 1024-byte aligned, SWIZZLE_128B, 32 f32 = 128 B
+// per swizzle row):
+//   Q  [D/32 chunks][128 rows][32]   K-major A operand of QK^T
+//   K  [D/32 chunks][BK keys][32]    K-major B operand of QK^T
+//   V  [D/32 chunks][BK keys][32]    MN-major B operand of PV (d contiguous)
+// TMEM columns: O at [0, D), S/P buffer b at [D + b*BK, D + (b+1)*BK).
+#include "fa_common.cuh"
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <math.h>
+#include <atomic>
+#include <mutex>
+
+namespace fa {
+namespace {
+
+constexpr int kBM = 128;            // query rows per CTA (MMA M)
+constexpr int kThreads = 256;       // 8 warps
+constexpr int kSoftmaxWarp0 = 4;    // warps 4..7
+constexpr float kRescaleLog2 = 8.f;  // lazy-rescale threshold (log2 units)
+
+template <int D, int BK, int NS>
+struct TcCfg {
+  static constexpr int kChunks = D / 32;
+  static constexpr int kQBytes = kBM * D * 4;
+  static constexpr int kKVBytes = BK * D * 4;
+  static constexpr int kOffQ = 0;
+  static constexpr int kOffK = kQBytes;
+  static constexpr int kOffV = kOffK + NS * kKVBytes;
+  static constexpr int kOffBar = kOffV + NS * kKVBytes;
+  static constexpr int kNumBars = 1 + 4 * NS + 2 + 2 + 1 + 1;
+  static constexpr int kSmemBytes = kOffBar + kNumBars * 8 + 16 + 1024;  // + align slack
+  static constexpr int kTmemColsUsed = D + 2 * BK;
+  static constexpr int kTmemCols = kTmemColsUsed <= 32 ? 32 : kTmemColsUsed <= 64 ? 64
+                                   : kTmemColsUsed <= 128 ? 128 : kTmemColsUsed <= 256 ? 256 : 512;
+  static_assert(D % 32 == 0 && D <= 128, "D must be a multiple of 32, at most 128");
+  static_assert(BK % 32 == 0 && BK <= 256, "BK must be a multiple of 32");
+  static_assert(kTmemColsUsed <= 512, "TMEM budget");
+};
+
+// ---- PTX wrappers ----------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait: returns false (and raises the CTA abort flag and the global
+// error word) if the phase does not complete within kWaitLimitNs, or if another
+// role already aborted.
+__device__ __noinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                       int* err) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = globaltimer_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 63u) == 0) {
+      if (*abort_flag) return false;
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        *abort_flag = 1;
+        atomicExch(err, (int)kErrTimeout);
+        return false;
+      }
+    }
+  }
+}
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
+                                            int x, int y, int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   bar)
+               : "memory");
+}
+// D[tmem] (+)= A[smem desc] * B[smem desc]
+__device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                       uint32_t idesc, uint32_t accum) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accum)
+      : "memory");
+}
+// D[tmem] (+)= A[tmem] * B[smem desc]
+__device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                       uint32_t idesc, uint32_t accum) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accum)
+      : "memory");
+}
+
+#define FA_R8(b) "=r"(r[b + 0]), "=r"(r[b + 1]), "=r"(r[b + 2]), "=r"(r[b + 3]), \
+                 "=r"(r[b + 4]), "=r"(r[b + 5]), "=r"(r[b + 6]), "=r"(r[b + 7])
+#define FA_W8(b) "r"(r[b + 0]), "r"(r[b + 1]), "r"(r[b + 2]), "r"(r[b + 3]), \
+                 "r"(r[b + 4]), "r"(r[b + 5]), "r"(r[b + 6]), "r"(r[b + 7])
+
+// 32 consecutive TMEM columns of this thread's lane -> registers.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : FA_R8(0), FA_R8(8), FA_R8(16), FA_R8(24)
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      FA_W8(0), FA_W8(8), FA_W8(16), FA_W8(24)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t to_tf32_rna(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return r;
+}
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Shared-memory matrix descriptor, SWIZZLE_128B, version 1 (sm_100).
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
+         ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (2ull << 61);
+}
+// Instruction descriptor, kind::tf32: D f32, A/B tf32, A K-major, B K- or MN-major.
+__host__ __device__ constexpr uint32_t instr_desc(int M, int N, bool b_mn_major) {
+  return (1u << 4) | (2u << 7) | (2u << 10) | ((b_mn_major ? 1u : 0u) << 16) |
+         ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+// ---- the kernel ------------------------------------------------------------
+template <int D, int BK, int NS>
+__global__ void __launch_bounds__(kThreads, 1)
+    tc_fwd_tf32(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                const __grid_constant__ CUtensorMap tmV, FwdParams p) {
+  using C = TcCfg<D, BK, NS>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t sQ = sbase + C::kOffQ;
+  const uint32_t sK = sbase + C::kOffK;
+  const uint32_t sV = sbase + C::kOffV;
+  const uint32_t bar0 = sbase + C::kOffBar;
+  // barrier addresses
+  const uint32_t bar_q_full = bar0;
+  auto bar_k_full = [&](int s) { return bar0 + 8u * (1 + s); };
+  auto bar_k_empty = [&](int s) { return bar0 + 8u * (1 + NS + s); };
+  auto bar_v_full = [&](int s) { return bar0 + 8u * (1 + 2 * NS + s); };
+  auto bar_v_empty = [&](int s) { return bar0 + 8u * (1 + 3 * NS + s); };
+  auto bar_s_full = [&](int b) { return bar0 + 8u * (1 + 4 * NS + b); };
+  auto bar_p_full = [&](int b) { return bar0 + 8u * (3 + 4 * NS + b); };
+  const uint32_t bar_o_done = bar0 + 8u * (5 + 4 * NS);
+  const uint32_t bar_drain = bar0 + 8u * (6 + 4 * NS);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kOffBar + C::kNumBars * 8);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int bh = blockIdx.x;
+  const int n_qt = gridDim.y;
+  const int qt = n_qt - 1 - (int)blockIdx.y;  // heaviest causal tiles dispatched first
+  const int q0 = qt * kBM;
+  const int q_rows = min(kBM, p.sq - q0);
+  int kend = p.sk;
+  if (p.causal) kend = causal_limit(p.q_offset + q0 + q_rows - 1, p.k_offset, p.sk);
+  const int n_kv = (kend + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    mbar_init(bar_q_full, 1);
+    for (int s = 0; s < NS; s++) {
+      mbar_init(bar_k_full(s), 1);
+      mbar_init(bar_k_empty(s), 1);
+      mbar_init(bar_v_full(s), 1);
+      mbar_init(bar_v_empty(s), 1);
+    }
+    for (int b = 0; b < 2; b++) {
+      mbar_init(bar_s_full(b), 1);
+      mbar_init(bar_p_full(b), 128);
+    }
+    mbar_init(bar_o_done, 1);
+    mbar_init(bar_drain, 1);
+    *abort_flag = (*(volatile int*)p.err != 0) ? 1 : 0;  // an earlier CTA failed: skip work
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"((uint32_t)C::kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t t_o = tmem;                       // O accumulator columns [0, D)
+  auto t_s = [&](int b) { return tmem + (uint32_t)(D + b * BK); };
+  const bool skip = *abort_flag != 0;
+
+  if (warp == 0) {
+    // ------------------------------ TMA producer
+    if (lane == 0 && !skip) {
+      mbar_expect_tx(bar_q_full, C::kQBytes);
+      for (int c = 0; c < C::kChunks; c++)
+        tma_load_3d(sQ + c * kBM * 128, &tmQ, bar_q_full, 32 * c, q0, bh);
+      int issued = 0;
+      bool ok = true;
+      for (int j = 0; j < n_kv && ok; j++) {
+        const int s = j % NS;
+        const uint32_t ph = (j / NS) & 1;
+        if (j >= NS) ok = mbar_wait(bar_k_empty(s), ph ^ 1, abort_flag, p.err);
+        if (!ok) break;
+        mbar_expect_tx(bar_k_full(s), C::kKVBytes);
+        for (int c = 0; c < C::kChunks; c++)
+          tma_load_3d(sK + s * C::kKVBytes + c * BK * 128, &tmK, bar_k_full(s), 32 * c, j * BK, bh);
+        if (j >= NS) ok = mbar_wait(bar_v_empty(s), ph ^ 1, abort_flag, p.err);
+        if (!ok) {  // K was issued: let it land before the CTA can exit
+          mbar_wait(bar_k_full(s), ph, abort_flag, p.err);
+          break;
+        }
+        mbar_expect_tx(bar_v_full(s), C::kKVBytes);
+        for (int c = 0; c < C::kChunks; c++)
+          tma_load_3d(sV + s * C::kKVBytes + c * BK * 128, &tmV, bar_v_full(s), 32 * c, j * BK, bh);
+        issued = j + 1;
+      }
+      {
+        // Wait (bounded, ignoring the abort flag) for the last load of every
+        // slot, so no TMA write can land after the CTA exits even when a
+        // consumer role aborted.  On the normal path these have all completed.
+        volatile int no_abort = 0;
+        mbar_wait(bar_q_full, 0, &no_abort, p.err);
+        for (int j = max(0, issued - NS); j < issued; j++) {
+          mbar_wait(bar_k_full(j % NS), (j / NS) & 1, &no_abort, p.err);
+          mbar_wait(bar_v_full(j % NS), (j / NS) & 1, &no_abort, p.err);
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------ MMA issuer
+    if (lane == 0 && !skip) {
+      constexpr uint32_t idesc_qk = instr_desc(kBM, BK, false);
+      constexpr uint32_t idesc_pv = instr_desc(kBM, D, true);
+      bool ok = mbar_wait(bar_q_full, 0, abort_flag, p.err);
+      tc_fence_after();
+      auto issue_pv = [&](int jj) -> bool {
+        const int s = jj % NS, b = jj & 1;
+        if (!mbar_wait(bar_p_full(b), (jj >> 1) & 1, abort_flag, p.err)) return false;
+        if (!mbar_wait(bar_v_full(s), (jj / NS) & 1, abort_flag, p.err)) return false;
+        tc_fence_after();
+        const uint32_t vbase = sV + s * C::kKVBytes;
+#pragma unroll
+        for (int kk = 0; kk < BK / 8; kk++) {
+          const uint64_t bdesc = smem_desc(vbase + kk * 1024, BK * 128, 1024);
+          mma_ts(t_o, t_s(b) + kk * 8, bdesc, idesc_pv, (jj > 0 || kk > 0) ? 1u : 0u);
+        }
+        tc_commit(bar_v_empty(s));
+        tc_commit(bar_o_done);
+        return true;
+      };
+      for (int j = 0; j < n_kv && ok; j++) {
+        const int s = j % NS, b = j & 1;
+        ok = mbar_wait(bar_k_full(s), (j / NS) & 1, abort_flag, p.err);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t kbase = sK + s * C::kKVBytes;
+#pragma unroll
+        for (int kk = 0; kk < D / 8; kk++) {
+          const uint32_t off = (kk >> 2) * 0u + (kk & 3) * 32;
+          const uint64_t adesc = smem_desc(sQ + (kk >> 2) * kBM * 128 + off, 16, 1024);
+          const uint64_t bdesc = smem_desc(kbase + (kk >> 2) * BK * 128 + off, 16, 1024);
+          mma_ss(t_s(b), adesc, bdesc, idesc_qk, kk > 0 ? 1u : 0u);
+        }
+        tc_commit(bar_s_full(b));
+        tc_commit(bar_k_empty(s));
+        if (j > 0) ok = issue_pv(j - 1);
+      }
+      if (ok && n_kv > 0) issue_pv(n_kv - 1);
+      // Drain: all MMAs issued by this thread complete before TMEM is freed.
+      tc_commit(bar_drain);
+      volatile int no_abort = 0;
+      mbar_wait(bar_drain, 0, &no_abort, p.err);
+    }
+    __syncwarp();
+  } else if (warp >= kSoftmaxWarp0) {
+    // ------------------------------ softmax warpgroup: thread = query row
+    const int quarter = warp - kSoftmaxWarp0;  // == warp % 4: TMEM lanes 32*quarter..
+    const int r = quarter * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const long long qg = p.q_offset + q0 + r;
+    float m = -INFINITY;  // running max in log2 units (possibly stale by < 2^8)
+    float l = 0.0f;
+    bool ok = !skip;
+    for (int j = 0; j < n_kv && ok; j++) {
+      const int b = j & 1;
+      ok = __all_sync(0xffffffffu, mbar_wait(bar_s_full(b), (j >> 1) & 1, abort_flag, p.err));
+      if (!ok) break;
+      tc_fence_after();
+      float x[BK];
+#pragma unroll
+      for (int c = 0; c < BK / 32; c++) {
+        uint32_t rr[32];
+        tmem_ld32(t_s(b) + lane_off + c * 32, rr);
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 32; e++) x[c * 32 + e] = __uint_as_float(rr[e]);
+      }
+      // visible keys of this row in tile j: [0, lim)
+      const int kbase = j * BK;
+      int lim = min(BK, p.sk - kbase);
+      if (p.causal) lim = min(lim, causal_limit(qg, p.k_offset + kbase, BK));
+      float mx = -INFINITY;
+#pragma unroll
+      for (int e = 0; e < BK; e++) {
+        x[e] = (e < lim) ? x[e] * p.scale_log2 : -INFINITY;
+        mx = fmaxf(mx, x[e]);
+      }
+      const float m_new = fmaxf(m, mx);
+      float corr = 1.0f;
+      bool need = false;
+      if (m == -INFINITY) {
+        m = m_new;  // nothing accumulated yet (O holds zeros or nothing)
+      } else if (m_new > m + kRescaleLog2) {
+        need = true;
+        corr = ex2(m - m_new);
+        m = m_new;
+      }
+      if (__any_sync(0xffffffffu, need)) {
+        // O is being accumulated by PV_{j-1}: wait for it, then rescale in TMEM.
+        ok = __all_sync(0xffffffffu, mbar_wait(bar_o_done, (j - 1) & 1, abort_flag, p.err));
+        if (!ok) break;
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < D / 32; c++) {
+          uint32_t rr[32];
+          tmem_ld32(t_o + lane_off + c * 32, rr);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; e++) rr[e] = __float_as_uint(__uint_as_float(rr[e]) * corr);
+          tmem_st32(t_o + lane_off + c * 32, rr);
+        }
+        l *= corr;
+      }
+      const bool any_visible = (m != -INFINITY);
+      float rowsum = 0.0f;
+#pragma unroll
+      for (int c = 0; c < BK / 32; c++) {
+        uint32_t rr[32];
+#pragma unroll
+        for (int e = 0; e < 32; e++) {
+          float pe = any_visible ? ex2(x[c * 32 + e] - m) : 0.0f;
+          uint32_t t = to_tf32_rna(pe);
+          rowsum += __uint_as_float(t);
+          rr[e] = t;
+        }
+        tmem_st32(t_s(b) + lane_off + c * 32, rr);
+      }
+      l += rowsum;
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(bar_p_full(b));
+    }
+    // epilogue: out = O / l, lse = ln(sum exp(s)) = (m + log2 l) * ln 2
+    if (n_kv > 0) {
+      const bool w = ok ? mbar_wait(bar_o_done, (n_kv - 1) & 1, abort_flag, p.err) : false;
+      ok = __all_sync(0xffffffffu, w);
+    }
+    if (ok) {
+      tc_fence_after();
+      const float inv_l = l > 0.0f ? 1.0f / l : 0.0f;
+      const bool row_ok = r < q_rows;
+      float* orow = p.o + ((size_t)bh * p.sq + q0 + r) * D;
+#pragma unroll
+      for (int c = 0; c < D / 32; c++) {
+        uint32_t rr[32];
+        if (n_kv > 0) {
+          tmem_ld32(t_o + lane_off + c * 32, rr);
+          tmem_wait_ld();
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; e++) rr[e] = 0u;
+        }
+        if (row_ok) {
+#pragma unroll
+          for (int e = 0; e < 32; e += 4) {
+            float4 v4 = make_float4(__uint_as_float(rr[e]) * inv_l, __uint_as_float(rr[e + 1]) * inv_l,
+                                    __uint_as_float(rr[e + 2]) * inv_l,
+                                    __uint_as_float(rr[e + 3]) * inv_l);
+            *reinterpret_cast<float4*>(orow + c * 32 + e) = v4;
+          }
+        }
+      }
+      if (row_ok && p.lse)
+        p.lse[(size_t)bh * p.sq + q0 + r] =
+            l > 0.0f ? (m + __log2f(l)) * 0.69314718055994530942f : -INFINITY;
+    }
+    tc_fence_before();
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"((uint32_t)C::kTmemCols)
+                 : "memory");
+  }
+}
+
+// ---- host side -------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+// 3-D map over [bh][seq][d] f32, box = 32 f32 x rows x 1, 128-byte swizzle.
+bool make_map(CUtensorMap* map, const float* base, int d, int seq, int bh, int rows) {
+  auto fn = get_encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[3] = {(cuuint64_t)d, (cuuint64_t)seq, (cuuint64_t)bh};
+  cuuint64_t strides[2] = {(cuuint64_t)d * 4, (cuuint64_t)seq * d * 4};
+  cuuint32_t box[3] = {32, (cuuint32_t)rows, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims,
+                  strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+template <int D, int BK, int NS>
+cudaError_t launch_tf32(const FwdParams& p, cudaStream_t s) {
+  using C = TcCfg<D, BK, NS>;
+  CUtensorMap mq, mk, mv;
+  if (!make_map(&mq, p.q, D, p.sq, p.bh, kBM) || !make_map(&mk, p.k, D, p.sk, p.bh, BK) ||
+      !make_map(&mv, p.v, D, p.sk, p.bh, BK))
+    return cudaErrorInvalidValue;
+  static std::atomic<unsigned long long> attr_set{0};  // one bit per device
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (!(attr_set.load() & bit)) {
+    cudaError_t e = cudaFuncSetAttribute(tc_fwd_tf32<D, BK, NS>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         C::kSmemBytes);
+    if (e != cudaSuccess) return e;
+    attr_set.fetch_or(bit);
+  }
+  const int n_qt = (p.sq + kBM - 1) / kBM;
+  dim3 grid(p.bh, n_qt);
+  tc_fwd_tf32<D, BK, NS><<<grid, kThreads, C::kSmemBytes, s>>>(mq, mk, mv, p);
+  count_launch();
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+bool tc_supported(int d, int precision) {
+  return precision == 0 && (d == 64 || d == 128);
+}
+
+size_t tc_scratch_floats(const FwdParams&, int) { return 0; }
+
+cudaError_t launch_tc(const FwdParams& p, int precision, float*, size_t, cudaStream_t s) {
+  if (precision != 0) return cudaErrorInvalidValue;
+  if (p.sq > 65535 * kBM) return cudaErrorInvalidValue;
+  if (p.d == 128) return launch_tf32<128, 64, 2>(p, s);
+  if (p.d == 64) return launch_tf32<64, 128, 2>(p, s);
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace fa

@@ -1,0 +1,106 @@
+"""CPU-side checks of the C ABI: the library loads, exports every function the
+header declares, and applies the crate's argument semantics (shape panics,
+zero-dimension early return) before touching any device.  No compute call is
+made here; without a GPU the compute calls must fail loudly (no CPU path)."""
+import ctypes
+import os
+import re
+
+import numpy as np
+import pytest
+
+import fa_b200
+from fa_cases import random_vec
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "fa_b200.h")
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"FA_API\s+[\w\s\*]+?\b(fa_\w+)\s*\(", text)))
+
+
+def test_header_declares_the_crate_api():
+    names = declared_functions()
+    for n in ("fa_flash_attention_v1", "fa_flash_attention_v2", "fa_flash_attention_v3",
+              "fa_flash_attention", "fa_flash_attention_multihead_v1",
+              "fa_flash_attention_multihead_v2", "fa_flash_attention_multihead_v3",
+              "fa_flash_attention_multihead", "fa_config_default"):
+        assert n in names
+
+
+def test_library_exports_every_declared_symbol():
+    lib = ctypes.CDLL(fa_b200.lib_path())
+    missing = [n for n in declared_functions() if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_config_default_mirrors_crate():
+    c = fa_b200._load().fa_config_default()
+    assert (c.block_size_q, c.block_size_kv, c.causal) == (64, 128, 0)
+    py = fa_b200.FlashAttentionConfig()
+    assert (py.block_size_q, py.block_size_kv, py.causal) == (64, 128, False)
+
+
+@pytest.mark.parametrize("which", ["q", "k", "v", "out"])
+@pytest.mark.parametrize("fn", [fa_b200.flash_attention_v1, fa_b200.flash_attention_v2,
+                                fa_b200.flash_attention_v3, fa_b200.flash_attention])
+def test_shape_mismatch_panics(fn, which):
+    # tests/correctness.rs:396-433: each of q/k/v/out one element short panics.
+    sq, sk, d = 4, 4, 8
+    bufs = {"q": random_vec(sq * d, 1), "k": random_vec(sk * d, 2), "v": random_vec(sk * d, 3),
+            "out": np.zeros(sq * d, np.float32)}
+    bufs[which] = np.ascontiguousarray(bufs[which][:-1])
+    with pytest.raises(fa_b200.Panic, match=f"{which} shape mismatch"):
+        fn(bufs["q"], bufs["k"], bufs["v"], sq, sk, d, fa_b200.FlashAttentionConfig(), bufs["out"])
+
+
+@pytest.mark.parametrize("fn", [fa_b200.flash_attention_multihead_v1,
+                                fa_b200.flash_attention_multihead_v2,
+                                fa_b200.flash_attention_multihead_v3,
+                                fa_b200.flash_attention_multihead])
+def test_multihead_shape_mismatch_panics(fn):
+    # tests/correctness.rs:435-459
+    b, h, sq, sk, d = 2, 2, 4, 4, 8
+    q = random_vec(b * h * sq * d, 1)[:-1].copy()
+    k, v = random_vec(b * h * sk * d, 2), random_vec(b * h * sk * d, 3)
+    out = np.zeros(b * h * sq * d, np.float32)
+    with pytest.raises(fa_b200.Panic):
+        fn(q, k, v, b, h, sq, sk, d, fa_b200.FlashAttentionConfig(), out)
+
+
+def test_zero_sized_dimensions_leave_out_untouched():
+    # tests/correctness.rs:461-504 -- returns before any device is needed.
+    d = 8
+    cfg = fa_b200.FlashAttentionConfig()
+    e = np.zeros(0, np.float32)
+    out = np.zeros(0, np.float32)
+    fa_b200.flash_attention_v2(e, random_vec(4 * d, 2), random_vec(4 * d, 3), 0, 4, d, cfg, out)
+    out2 = np.full(4 * d, 12.5, np.float32)
+    fa_b200.flash_attention_v2(random_vec(4 * d, 4), e, e, 4, 0, d, cfg, out2)
+    assert np.all(out2 == 12.5)
+    fa_b200.flash_attention_v2(e, e, e, 4, 4, 0, cfg, out)
+
+
+def test_no_device_fails_loudly():
+    if fa_b200.device_count() > 0:
+        pytest.skip("a GPU is present")
+    d = 8
+    out = np.zeros(4 * d, np.float32)
+    with pytest.raises(fa_b200.FaError, match="FA_ERR_NO_DEVICE"):
+        fa_b200.flash_attention_v2(random_vec(4 * d, 1), random_vec(4 * d, 2),
+                                   random_vec(4 * d, 3), 4, 4, d,
+                                   fa_b200.FlashAttentionConfig(), out)
+
+
+def test_precision_control():
+    old = fa_b200.get_precision()
+    try:
+        for p in (fa_b200.PREC_TF32, fa_b200.PREC_3XTF32, fa_b200.PREC_FP32):
+            fa_b200.set_precision(p)
+            assert fa_b200.get_precision() == p
+        with pytest.raises(fa_b200.FaError):
+            fa_b200.set_precision(7)
+    finally:
+        fa_b200.set_precision(old)

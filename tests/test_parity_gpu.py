@@ -1,0 +1,243 @@
+"""GPU parity: the C ABI on a B200 against the CPU oracle on identical inputs.
+
+Tolerances (max abs error vs the oracle, output and row LSE):
+  TF32   (tcgen05 kind::tf32)         2e-3
+  3xTF32 (error-compensated default)  2e-5
+  FP32   (CUDA-core f32)              2e-5
+plus the crate's own assertion of every case against its naive oracle, 1e-3
+(tests/correctness.rs:109-112).
+"""
+import numpy as np
+import pytest
+
+import oracle as O
+from fa_cases import (AGREEMENT_CASES, BASELINE_CONFIGS, REFERENCE_CASES, TC_CASES,
+                      baseline_inputs, max_abs_diff, random_vec)
+
+pytestmark = pytest.mark.gpu
+
+TOL = {0: 2e-3, 1: 2e-5, 2: 2e-5}
+PRECISIONS = [0, 1, 2]
+
+
+@pytest.fixture
+def fa(gpu_lib):
+    old = gpu_lib.get_precision()
+    yield gpu_lib
+    gpu_lib.set_precision(old)
+
+
+def run_single(fa, q, k, v, sq, sk, d, br, bc, causal, fn=None):
+    out = np.zeros(sq * d, np.float32)
+    (fn or fa.flash_attention_v2)(q, k, v, sq, sk, d,
+                                  fa.FlashAttentionConfig(br, bc, causal), out)
+    return out
+
+
+@pytest.mark.parametrize("prec", PRECISIONS)
+@pytest.mark.parametrize("case", REFERENCE_CASES)
+def test_reference_matrix(fa, prec, case):
+    sq, sk, d, br, bc, causal = case
+    fa.set_precision(prec)
+    q, k, v = random_vec(sq * d, 1), random_vec(sk * d, 2), random_vec(sk * d, 3)
+    out = run_single(fa, q, k, v, sq, sk, d, br, bc, causal)
+    want, _ = O.flash_v2(q, k, v, sq, sk, d, causal, br, bc)
+    assert max_abs_diff(out, want) < TOL[prec], fa.last_path()
+    assert max_abs_diff(out, O.naive_f32(q, k, v, sq, sk, d, causal)) < 1e-3
+
+
+@pytest.mark.parametrize("prec", PRECISIONS)
+@pytest.mark.parametrize("case", TC_CASES)
+def test_tensor_core_shapes_with_lse(fa, prec, case):
+    sq, sk, d, causal = case
+    fa.set_precision(prec)
+    rng = np.random.default_rng(sq * 7919 + sk * 31 + d)
+    q = rng.standard_normal(sq * d, dtype=np.float32)
+    k = rng.standard_normal(sk * d, dtype=np.float32)
+    v = rng.standard_normal(sk * d, dtype=np.float32)
+    out, lse = fa.multihead_lse(q, k, v, 1, sq, sk, d, causal)
+    path = fa.last_path()
+    want, wlse = O.flash_v2(q, k, v, sq, sk, d, causal)
+    assert max_abs_diff(out, want) < TOL[prec], path
+    assert max_abs_diff(lse, wlse) < TOL[prec], path
+    if prec == 0 and sq > 16:
+        assert path == "tcgen05_tf32"
+
+
+@pytest.mark.parametrize("prec", PRECISIONS)
+def test_multihead_matches_per_head_naive(fa, prec):
+    fa.set_precision(prec)
+    b, h, sq, sk, d = 2, 3, 37, 50, 16
+    q = random_vec(b * h * sq * d, 21)
+    k = random_vec(b * h * sk * d, 22)
+    v = random_vec(b * h * sk * d, 23)
+    cfg = fa.FlashAttentionConfig(8, 12, True)
+    for fn in (fa.flash_attention_multihead_v1, fa.flash_attention_multihead_v2,
+               fa.flash_attention_multihead_v3, fa.flash_attention_multihead):
+        out = np.zeros(b * h * sq * d, np.float32)
+        fn(q, k, v, b, h, sq, sk, d, cfg, out)
+        for bh in range(b * h):
+            sl_q = slice(bh * sq * d, (bh + 1) * sq * d)
+            sl_k = slice(bh * sk * d, (bh + 1) * sk * d)
+            want = O.naive_f32(q[sl_q], k[sl_k], v[sl_k], sq, sk, d, True)
+            assert max_abs_diff(out[sl_q], want) < 1e-3
+
+
+@pytest.mark.parametrize("br,bc", [(64, 128), (32, 32), (1024, 1024), (1, 1)])
+def test_causal_first_query_equals_first_value_row(fa, br, bc):
+    # tests/correctness.rs:240-263 at the library's default precision (3xTF32): 1e-5.
+    fa.set_precision(fa.PREC_3XTF32)
+    s, d = 256, 64
+    q, k, v = random_vec(s * d, 30), random_vec(s * d, 31), random_vec(s * d, 32)
+    for fn in (fa.flash_attention_v1, fa.flash_attention_v2, fa.flash_attention_v3):
+        out = run_single(fa, q, k, v, s, s, d, br, bc, True, fn)
+        assert max_abs_diff(out[:d], v[:d]) < 1e-5
+
+
+def test_causal_first_query_tf32_within_tf32_rounding(fa):
+    # In TF32 mode V is rounded to 10 mantissa bits, so row 0 equals V[0] only
+    # to TF32 precision (the reason the default precision is 3xTF32).
+    fa.set_precision(fa.PREC_TF32)
+    s, d = 256, 64
+    q, k, v = random_vec(s * d, 30), random_vec(s * d, 31), random_vec(s * d, 32)
+    out = run_single(fa, q, k, v, s, s, d, 64, 128, True)
+    assert max_abs_diff(out[:d], v[:d]) < 2e-3
+
+
+@pytest.mark.parametrize("prec", PRECISIONS)
+def test_output_is_finite(fa, prec):
+    fa.set_precision(prec)
+    sq, sk, d = 40, 40, 32
+    out = run_single(fa, random_vec(sq * d, 10), random_vec(sk * d, 11), random_vec(sk * d, 12),
+                     sq, sk, d, 64, 128, True)
+    assert np.all(np.isfinite(out))
+
+
+@pytest.mark.parametrize("case", AGREEMENT_CASES)
+def test_v1_v2_v3_agree(fa, case):
+    # tests/correctness.rs:295-375 demands v2 == v3 within 1e-5; on the GPU the
+    # three run the same kernels, so they agree bit for bit.
+    sq, sk, d, br, bc, causal = case
+    q, k, v = random_vec(sq * d, 1), random_vec(sk * d, 2), random_vec(sk * d, 3)
+    outs = [run_single(fa, q, k, v, sq, sk, d, br, bc, causal, fn)
+            for fn in (fa.flash_attention_v1, fa.flash_attention_v2, fa.flash_attention_v3)]
+    assert np.array_equal(outs[0], outs[1]) and np.array_equal(outs[1], outs[2])
+
+
+def test_zero_block_size_is_clamped(fa):
+    sq, sk, d = 23, 29, 16
+    q, k, v = random_vec(sq * d, 1), random_vec(sk * d, 2), random_vec(sk * d, 3)
+    for causal in (False, True):
+        out = run_single(fa, q, k, v, sq, sk, d, 0, 0, causal)
+        assert max_abs_diff(out, O.naive_f32(q, k, v, sq, sk, d, causal)) < 1e-3
+
+
+def test_block_size_does_not_change_results(fa):
+    sq, sk, d = 200, 200, 128
+    q, k, v = random_vec(sq * d, 1), random_vec(sk * d, 2), random_vec(sk * d, 3)
+    a = run_single(fa, q, k, v, sq, sk, d, 64, 128, True)
+    for br, bc in ((1, 1), (7, 3), (1024, 1024)):
+        assert np.array_equal(a, run_single(fa, q, k, v, sq, sk, d, br, bc, True))
+
+
+@pytest.mark.parametrize("sq,sk,d,causal", [
+    (1, 32768, 128, False), (1, 5000, 64, True), (4, 3000, 128, True), (16, 2049, 256, False),
+    (3, 1000, 36, False), (8, 100000, 128, False), (2, 7, 128, False)])
+def test_decode_split_kv(fa, sq, sk, d, causal):
+    bh = 3
+    rng = np.random.default_rng(sq + sk + d)
+    q = rng.standard_normal(bh * sq * d, dtype=np.float32)
+    k = rng.standard_normal(bh * sk * d, dtype=np.float32)
+    v = rng.standard_normal(bh * sk * d, dtype=np.float32)
+    out, lse = fa.multihead_lse(q, k, v, bh, sq, sk, d, causal)
+    assert fa.last_path() == "decode_splitkv"
+    want, wlse, _ = O.flash_v2_multihead(q, k, v, bh, sq, sk, d, causal)
+    assert max_abs_diff(out, want) < 2e-5
+    assert max_abs_diff(lse, wlse) < 2e-5
+
+
+@pytest.mark.parametrize("prec", [0, 1])
+@pytest.mark.parametrize("name", ["c1", "c3", "c4"])
+def test_baseline_configs(fa, prec, name):
+    fa.set_precision(prec)
+    bh_override = 16 if name == "c3" else None  # c3: 16 of its 256 slices (same shape)
+    q, k, v, (bh, sq, sk, d, causal) = baseline_inputs(name, bh_override)
+    out, lse = fa.multihead_lse(q, k, v, bh, sq, sk, d, causal)
+    want, wlse, _ = O.flash_v2_multihead(q, k, v, bh, sq, sk, d, causal)
+    tol = 2e-5 if name == "c4" else TOL[prec]  # c4 runs the exact-f32 decode kernel
+    assert max_abs_diff(out, want) < tol
+    assert max_abs_diff(lse, wlse) < tol
+
+
+@pytest.mark.parametrize("prec", [0, 1])
+def test_baseline_c2_full_run_sampled_heads(fa, prec):
+    fa.set_precision(prec)
+    q, k, v, (bh, sq, sk, d, causal) = baseline_inputs("c2")
+    out, lse = fa.multihead_lse(q, k, v, bh, sq, sk, d, causal)
+    for h in (0, 13, bh - 1):
+        sq_sl = slice(h * sq * d, (h + 1) * sq * d)
+        sk_sl = slice(h * sk * d, (h + 1) * sk * d)
+        want, wlse, _ = O.flash_v2_multihead(q[sq_sl], k[sk_sl], v[sk_sl], 1, sq, sk, d, causal)
+        assert max_abs_diff(out[sq_sl], want) < TOL[prec]
+        assert max_abs_diff(lse[h * sq:(h + 1) * sq], wlse) < TOL[prec]
+
+
+def test_baseline_c5_single_gpu_sampled_rows(fa):
+    # 1 x 131072 x 128 causal on one GPU; rows checked against the f64 naive.
+    fa.set_precision(fa.PREC_TF32)
+    q, k, v, (bh, sq, sk, d, causal) = baseline_inputs("c5")
+    out, lse = fa.multihead_lse(q, k, v, bh, sq, sk, d, causal)
+    assert np.all(np.isfinite(out))
+    for r in (0, 1, 127, 128, 4097, 65535, 100000, sq - 1):
+        w, wl = O.naive_f64(q, k, v, sq, sk, d, causal, r, r + 1)
+        assert max_abs_diff(out[r * d:(r + 1) * d], w) < 2e-3
+        assert abs(float(lse[r]) - float(wl[0])) < 2e-3
+
+
+def test_device_api_matches_host_api(fa):
+    import torch
+    fa.set_precision(fa.PREC_TF32)
+    bh, sq, sk, d = 4, 300, 500, 128
+    q, k, v = (random_vec(bh * sq * d, 1), random_vec(bh * sk * d, 2),
+               random_vec(bh * sk * d, 3))
+    host, hlse = fa.multihead_lse(q, k, v, bh, sq, sk, d, True)
+    dq = torch.from_numpy(q).cuda().view(bh, sq, d)
+    dk = torch.from_numpy(k).cuda().view(bh, sk, d)
+    dv = torch.from_numpy(v).cuda().view(bh, sk, d)
+    out = torch.empty_like(dq)
+    lse = torch.empty(bh, sq, device="cuda")
+    n0 = fa.launch_count()
+    fa.forward_device(dq, dk, dv, out, lse, causal=True)
+    fa.sync_status()
+    assert fa.launch_count() > n0
+    assert np.array_equal(out.cpu().numpy().ravel(), host)
+    assert np.array_equal(lse.cpu().numpy().ravel(), hlse)
+
+
+@pytest.mark.parametrize("prec", [0, 2])
+def test_partial_ranges_and_lse_combine(fa, prec):
+    # The KV-range split used across GPUs, emulated on one GPU: three key
+    # ranges (one entirely in some rows' future), merged by the LSE combine.
+    import torch
+    fa.set_precision(prec)
+    bh, s, d = 2, 700, 128
+    q, k, v = random_vec(bh * s * d, 4), random_vec(bh * s * d, 5), random_vec(bh * s * d, 6)
+    want, wlse, _ = O.flash_v2_multihead(q, k, v, bh, s, s, d, True)
+    dq = torch.from_numpy(q).cuda().view(bh, s, d)
+    dk = torch.from_numpy(k).cuda().view(bh, s, d)
+    dv = torch.from_numpy(v).cuda().view(bh, s, d)
+    bounds = [0, 256, 400, s]
+    parts_o = torch.empty(len(bounds) - 1, bh, s, d, device="cuda")
+    parts_l = torch.empty(len(bounds) - 1, bh, s, device="cuda")
+    for i in range(len(bounds) - 1):
+        a, b = bounds[i], bounds[i + 1]
+        fa.forward_partial_device(dq, dk[:, a:b].contiguous(), dv[:, a:b].contiguous(),
+                                  parts_o[i], parts_l[i], True, 0, a)
+    out = torch.empty(bh * s, d, device="cuda")
+    lse = torch.empty(bh * s, device="cuda")
+    fa.lse_combine_device(parts_o.view(len(bounds) - 1, bh * s, d),
+                          parts_l.view(len(bounds) - 1, bh * s), out, lse)
+    fa.sync_status()
+    tol = TOL[prec]
+    assert max_abs_diff(out.cpu().numpy().ravel(), want) < tol
+    assert max_abs_diff(lse.cpu().numpy().ravel(), wlse) < tol
