@@ -26,7 +26,6 @@ import statistics
 import subprocess
 import sys
 import tempfile
-import threading
 import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
@@ -65,7 +64,7 @@ def measured_peaks():
 
 class ClockSampler:
     """nvidia-smi clocks and throttle reasons sampled every 200 ms."""
-    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    QUERY = ("timestamp,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
@@ -94,7 +93,11 @@ class ClockSampler:
             except subprocess.TimeoutExpired:
                 self.proc.kill()
 
-    def summary(self):
+    def summary(self, t0=None, t1=None):
+        """Median SM clock and active throttle reasons of the samples taken
+        between wall times t0 and t1 (the timed region); if the region was too
+        short to hold a sample, of all samples (warm-up included)."""
+        import datetime
         rows = []
         try:
             with open(self.path) as f:
@@ -109,13 +112,26 @@ class ClockSampler:
                 os.unlink(self.path)
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+
+        def ts(r):
+            try:
+                return datetime.datetime.strptime(r[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+            except ValueError:
+                return None
+        window = "timed region"
+        if t0 is not None:
+            inside = [r for r in rows if ts(r) is not None and t0 <= ts(r) <= t1]
+            if inside:
+                rows = inside
+            else:
+                window = "warm-up + timed region (timed region shorter than one sample)"
         sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
         mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i] == "Active"})
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
-                "samples": len(rows)}
+                "samples": len(rows), "window": window}
 
 
 def cpu_baseline(cfg, budget_s=12.0):
@@ -218,7 +234,7 @@ def config_dict(args, cfg, world):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--config", default="c2", choices=sorted(CONFIGS))
@@ -262,6 +278,8 @@ def main():
             flush.fill_(1.0)
         fa_b200.forward_device(q, k, v, out, lse, causal=causal, stream=stream)
 
+    clk = ClockSampler(local).__enter__()
+    time.sleep(0.3)  # let nvidia-smi take its first sample
     for _ in range(args.warmup):
         step()
     fa_b200.sync_status(stream)
@@ -274,18 +292,21 @@ def main():
         dist.barrier()
     torch.cuda.synchronize()
     launches0 = fa_b200.launch_count()
-    with ClockSampler(local) as clk:
-        t_start = torch.cuda.Event(enable_timing=True)
-        t_end = torch.cuda.Event(enable_timing=True)
-        t_start.record(stream)
-        for i in range(args.steps):
-            if flush is not None:
-                flush.fill_(1.0)
-            ev[i][0].record(stream)
-            fa_b200.forward_device(q, k, v, out, lse, causal=causal, stream=stream)
-            ev[i][1].record(stream)
-        t_end.record(stream)
-        torch.cuda.synchronize()
+    wall0 = time.time()
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    t_start.record(stream)
+    for i in range(args.steps):
+        if flush is not None:
+            flush.fill_(1.0)
+        ev[i][0].record(stream)
+        fa_b200.forward_device(q, k, v, out, lse, causal=causal, stream=stream)
+        ev[i][1].record(stream)
+    t_end.record(stream)
+    torch.cuda.synchronize()
+    wall1 = time.time()
+    time.sleep(0.25)
+    clk.__exit__(None, None, None)
     launches = fa_b200.launch_count() - launches0
     fa_b200.sync_status(stream)
     path = fa_b200.last_path()
@@ -299,7 +320,7 @@ def main():
     step_ms = float(t.item())
     fl = flops_of(bh, sq, sk, d, causal)
     value = world * fl / (step_ms * 1e-3) / 1e12
-    clocks = clk.summary()
+    clocks = clk.summary(wall0, wall1)
 
     # end-to-end through the public host-slice API (pinned host buffers,
     # H2D of Q/K/V and D2H of OUT inside the timed region, every step)

@@ -23,11 +23,16 @@
 // Causal runs never load or multiply key tiles wholly past the tile's last
 // row (src/v2.rs:210-212), and CTAs are dispatched heaviest-tile first.
 //
-// Shared-memory layouts (all 1024-byte aligned, SWIZZLE_128B, 32 f32 = 128 B
-// per swizzle row):
-//   Q  [D/32 chunks][128 rows][32]   K-major A operand of QK^T
-//   K  [D/32 chunks][BK keys][32]    K-major B operand of QK^T
-//   V  [D/32 chunks][BK keys][32]    MN-major B operand of PV (d contiguous)
+// Shared-memory layouts (all 1024-byte aligned, 32 f32 = 128 B per swizzle row):
+//   Q  [D/32 chunks][128 rows][32]   K-major A operand of QK^T, 128B swizzle
+//                                    (16-byte granules XOR row%8)
+//   K  [D/32 chunks][BK keys][32]    K-major B operand of QK^T, same swizzle
+//   V  [D/32 chunks][BK keys][32]    MN-major B operand of PV (d contiguous).
+//                                    An MN-major TF32 operand must use the
+//                                    "128B swizzle, 32B atom" layout (32-byte
+//                                    granules XOR row%4; K grouped by 4 rows,
+//                                    512 B apart), which TMA writes with
+//                                    CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B.
 // TMEM columns: O at [0, D), S/P buffer b at [D + b*BK, D + (b+1)*BK).
 #include "fa_common.cuh"
 
@@ -45,23 +50,29 @@ constexpr int kThreads = 256;       // 8 warps
 constexpr int kSoftmaxWarp0 = 4;    // warps 4..7
 constexpr float kRescaleLog2 = 8.f;  // lazy-rescale threshold (log2 units)
 
-template <int D, int BK, int NS>
+// D: head size.  BK: keys per K tile (the N of the QK^T MMA).  VK: keys per V
+// sub-tile (BK/VK sub-tiles per K tile, so V slots free up in finer steps).
+// NKS / NVS: depth of the K and V rings.
+template <int D, int BK, int VK, int NKS, int NVS>
 struct TcCfg {
   static constexpr int kChunks = D / 32;
-  static constexpr int kQBytes = kBM * D * 4;
-  static constexpr int kKVBytes = BK * D * 4;
-  static constexpr int kOffQ = 0;
-  static constexpr int kOffK = kQBytes;
-  static constexpr int kOffV = kOffK + NS * kKVBytes;
-  static constexpr int kOffBar = kOffV + NS * kKVBytes;
-  static constexpr int kNumBars = 1 + 4 * NS + 2 + 2 + 1 + 1;
+  static constexpr int kVS = BK / VK;
+  static constexpr int kKBytes = BK * D * 4;
+  static constexpr int kVBytes = VK * D * 4;
+  static constexpr int kOffK = 0;
+  static constexpr int kOffV = kOffK + NKS * kKBytes;
+  static constexpr int kOffBar = kOffV + NVS * kVBytes;
+  static constexpr int kNumBars = 1 + 2 * NKS + 2 * NVS + 2 + 2 + 1 + 1 + 1;
   static constexpr int kSmemBytes = kOffBar + kNumBars * 8 + 16 + 1024;  // + align slack
-  static constexpr int kTmemColsUsed = D + 2 * BK;
+  // TMEM columns: Q [0, D), O [D, 2D), S/P buffers [2D, 2D + 2*BK)
+  static constexpr int kTmemColsUsed = 2 * D + 2 * BK;
   static constexpr int kTmemCols = kTmemColsUsed <= 32 ? 32 : kTmemColsUsed <= 64 ? 64
                                    : kTmemColsUsed <= 128 ? 128 : kTmemColsUsed <= 256 ? 256 : 512;
   static_assert(D % 32 == 0 && D <= 128, "D must be a multiple of 32, at most 128");
   static_assert(BK % 32 == 0 && BK <= 256, "BK must be a multiple of 32");
+  static_assert(BK % VK == 0 && VK % 8 == 0, "V sub-tiles must divide the K tile");
   static_assert(kTmemColsUsed <= 512, "TMEM budget");
+  static_assert(kSmemBytes <= 232448, "shared-memory budget");
 };
 
 // ---- PTX wrappers ----------------------------------------------------------
@@ -173,6 +184,16 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
 __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
+// tcgen05.ld writes its destination registers asynchronously; they are valid
+// only after tcgen05.wait::ld.  The compiler does not know that, so after the
+// wait every destination register is passed through an empty volatile asm:
+// volatile asms keep their order, and all later uses depend on these outputs.
+template <int N>
+__device__ __forceinline__ void tmem_wait_ld_regs(uint32_t (&r)[N]) {
+  tmem_wait_ld();
+#pragma unroll
+  for (int i = 0; i < N; i++) asm volatile("" : "+r"(r[i]));
+}
 __device__ __forceinline__ void tmem_wait_st() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
@@ -187,10 +208,13 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-// Shared-memory matrix descriptor, SWIZZLE_128B, version 1 (sm_100).
-__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+// Shared-memory matrix descriptor, version 1 (sm_100).  Layout type in bits
+// 61-63: 2 = 128B swizzle (16B granules), 1 = 128B swizzle with 32B granules.
+constexpr uint64_t kLayoutSw128 = 2, kLayoutSw128Base32 = 1;
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo,
+                                              uint64_t layout) {
   return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
-         ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (2ull << 61);
+         ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (layout << 61);
 }
 // Instruction descriptor, kind::tf32: D f32, A/B tf32, A K-major, B K- or MN-major.
 __host__ __device__ constexpr uint32_t instr_desc(int M, int N, bool b_mn_major) {
@@ -199,29 +223,42 @@ __host__ __device__ constexpr uint32_t instr_desc(int M, int N, bool b_mn_major)
 }
 
 // ---- the kernel ------------------------------------------------------------
-template <int D, int BK, int NS>
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+template <int D, int BK, int VK, int NKS, int NVS>
 __global__ void __launch_bounds__(kThreads, 1)
-    tc_fwd_tf32(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                const __grid_constant__ CUtensorMap tmV, FwdParams p) {
-  using C = TcCfg<D, BK, NS>;
+    tc_fwd_tf32(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                FwdParams p) {
+  using C = TcCfg<D, BK, VK, NKS, NVS>;
+  constexpr int VS = C::kVS;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
-  const uint32_t sQ = sbase + C::kOffQ;
   const uint32_t sK = sbase + C::kOffK;
   const uint32_t sV = sbase + C::kOffV;
   const uint32_t bar0 = sbase + C::kOffBar;
-  // barrier addresses
-  const uint32_t bar_q_full = bar0;
+  const uint32_t bar_q_full = bar0;  // Q staged in TMEM by the softmax warps
   auto bar_k_full = [&](int s) { return bar0 + 8u * (1 + s); };
-  auto bar_k_empty = [&](int s) { return bar0 + 8u * (1 + NS + s); };
-  auto bar_v_full = [&](int s) { return bar0 + 8u * (1 + 2 * NS + s); };
-  auto bar_v_empty = [&](int s) { return bar0 + 8u * (1 + 3 * NS + s); };
-  auto bar_s_full = [&](int b) { return bar0 + 8u * (1 + 4 * NS + b); };
-  auto bar_p_full = [&](int b) { return bar0 + 8u * (3 + 4 * NS + b); };
-  const uint32_t bar_o_done = bar0 + 8u * (5 + 4 * NS);
-  const uint32_t bar_drain = bar0 + 8u * (6 + 4 * NS);
+  auto bar_k_empty = [&](int s) { return bar0 + 8u * (1 + NKS + s); };
+  auto bar_v_full = [&](int s) { return bar0 + 8u * (1 + 2 * NKS + s); };
+  auto bar_v_empty = [&](int s) { return bar0 + 8u * (1 + 2 * NKS + NVS + s); };
+  constexpr uint32_t kB2 = 1 + 2 * NKS + 2 * NVS;
+  auto bar_s_full = [&](int b) { return bar0 + 8u * (kB2 + b); };
+  auto bar_p_full = [&](int b) { return bar0 + 8u * (kB2 + 2 + b); };
+  // o_done completes once per PV.  A wait on it for PV_{j-1} at softmax step j
+  // is unambiguous: S_j was issued after PV_{j-2}, so when S_j is visible at
+  // most PV_{j-1} and PV_j remain, and PV_j cannot start before P_j exists.
+  const uint32_t bar_o_done = bar0 + 8u * (kB2 + 4);
+  const uint32_t bar_drain = bar0 + 8u * (kB2 + 5);
+  // Single-use barrier for "the last PV has completed".  The per-PV o_done
+  // barrier cannot serve the epilogue: when the softmax loop ends, the last two
+  // PVs may both be pending, and a parity wait cannot tell phase n from n-2.
+  const uint32_t bar_o_final = bar0 + 8u * (kB2 + 6);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kOffBar + C::kNumBars * 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -236,10 +273,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int n_kv = (kend + BK - 1) / BK;
 
   if (threadIdx.x == 0) {
-    mbar_init(bar_q_full, 1);
-    for (int s = 0; s < NS; s++) {
+    mbar_init(bar_q_full, 128);
+    for (int s = 0; s < NKS; s++) {
       mbar_init(bar_k_full(s), 1);
       mbar_init(bar_k_empty(s), 1);
+    }
+    for (int s = 0; s < NVS; s++) {
       mbar_init(bar_v_full(s), 1);
       mbar_init(bar_v_empty(s), 1);
     }
@@ -249,6 +288,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     mbar_init(bar_o_done, 1);
     mbar_init(bar_drain, 1);
+    mbar_init(bar_o_final, 1);
     *abort_flag = (*(volatile int*)p.err != 0) ? 1 : 0;  // an earlier CTA failed: skip work
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -264,46 +304,44 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t t_o = tmem;                       // O accumulator columns [0, D)
-  auto t_s = [&](int b) { return tmem + (uint32_t)(D + b * BK); };
+  const uint32_t t_q = tmem;                        // Q tile (A operand of QK^T)
+  const uint32_t t_o = tmem + (uint32_t)D;          // O accumulator
+  auto t_s = [&](int b) { return tmem + (uint32_t)(2 * D + b * BK); };
   const bool skip = *abort_flag != 0;
 
   if (warp == 0) {
-    // ------------------------------ TMA producer
+    // ------------------------------ TMA producer (K and V rings)
     if (lane == 0 && !skip) {
-      mbar_expect_tx(bar_q_full, C::kQBytes);
-      for (int c = 0; c < C::kChunks; c++)
-        tma_load_3d(sQ + c * kBM * 128, &tmQ, bar_q_full, 32 * c, q0, bh);
-      int issued = 0;
+      int issued_k = 0, issued_v = 0;
       bool ok = true;
       for (int j = 0; j < n_kv && ok; j++) {
-        const int s = j % NS;
-        const uint32_t ph = (j / NS) & 1;
-        if (j >= NS) ok = mbar_wait(bar_k_empty(s), ph ^ 1, abort_flag, p.err);
+        const int sk = j % NKS;
+        if (j >= NKS) ok = mbar_wait(bar_k_empty(sk), ((j / NKS) & 1) ^ 1, abort_flag, p.err);
         if (!ok) break;
-        mbar_expect_tx(bar_k_full(s), C::kKVBytes);
+        mbar_expect_tx(bar_k_full(sk), C::kKBytes);
         for (int c = 0; c < C::kChunks; c++)
-          tma_load_3d(sK + s * C::kKVBytes + c * BK * 128, &tmK, bar_k_full(s), 32 * c, j * BK, bh);
-        if (j >= NS) ok = mbar_wait(bar_v_empty(s), ph ^ 1, abort_flag, p.err);
-        if (!ok) {  // K was issued: let it land before the CTA can exit
-          mbar_wait(bar_k_full(s), ph, abort_flag, p.err);
-          break;
+          tma_load_3d(sK + sk * C::kKBytes + c * BK * 128, &tmK, bar_k_full(sk), 32 * c, j * BK, bh);
+        issued_k = j + 1;
+        for (int h = 0; h < VS && ok; h++) {
+          const int g = j * VS + h, sv = g % NVS;
+          if (g >= NVS) ok = mbar_wait(bar_v_empty(sv), ((g / NVS) & 1) ^ 1, abort_flag, p.err);
+          if (!ok) break;
+          mbar_expect_tx(bar_v_full(sv), C::kVBytes);
+          for (int c = 0; c < C::kChunks; c++)
+            tma_load_3d(sV + sv * C::kVBytes + c * VK * 128, &tmV, bar_v_full(sv), 32 * c, g * VK,
+                        bh);
+          issued_v = g + 1;
         }
-        mbar_expect_tx(bar_v_full(s), C::kKVBytes);
-        for (int c = 0; c < C::kChunks; c++)
-          tma_load_3d(sV + s * C::kKVBytes + c * BK * 128, &tmV, bar_v_full(s), 32 * c, j * BK, bh);
-        issued = j + 1;
       }
       {
         // Wait (bounded, ignoring the abort flag) for the last load of every
         // slot, so no TMA write can land after the CTA exits even when a
         // consumer role aborted.  On the normal path these have all completed.
         volatile int no_abort = 0;
-        mbar_wait(bar_q_full, 0, &no_abort, p.err);
-        for (int j = max(0, issued - NS); j < issued; j++) {
-          mbar_wait(bar_k_full(j % NS), (j / NS) & 1, &no_abort, p.err);
-          mbar_wait(bar_v_full(j % NS), (j / NS) & 1, &no_abort, p.err);
-        }
+        for (int j = max(0, issued_k - NKS); j < issued_k; j++)
+          mbar_wait(bar_k_full(j % NKS), (j / NKS) & 1, &no_abort, p.err);
+        for (int g = max(0, issued_v - NVS); g < issued_v; g++)
+          mbar_wait(bar_v_full(g % NVS), (g / NVS) & 1, &no_abort, p.err);
       }
     }
     __syncwarp();
@@ -315,38 +353,44 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = mbar_wait(bar_q_full, 0, abort_flag, p.err);
       tc_fence_after();
       auto issue_pv = [&](int jj) -> bool {
-        const int s = jj % NS, b = jj & 1;
+        const int b = jj & 1;
         if (!mbar_wait(bar_p_full(b), (jj >> 1) & 1, abort_flag, p.err)) return false;
-        if (!mbar_wait(bar_v_full(s), (jj / NS) & 1, abort_flag, p.err)) return false;
-        tc_fence_after();
-        const uint32_t vbase = sV + s * C::kKVBytes;
 #pragma unroll
-        for (int kk = 0; kk < BK / 8; kk++) {
-          const uint64_t bdesc = smem_desc(vbase + kk * 1024, BK * 128, 1024);
-          mma_ts(t_o, t_s(b) + kk * 8, bdesc, idesc_pv, (jj > 0 || kk > 0) ? 1u : 0u);
+        for (int h = 0; h < VS; h++) {
+          const int g = jj * VS + h, sv = g % NVS;
+          if (!mbar_wait(bar_v_full(sv), (g / NVS) & 1, abort_flag, p.err)) return false;
+          tc_fence_after();
+          const uint32_t vbase = sV + sv * C::kVBytes;
+#pragma unroll
+          for (int kk = 0; kk < VK / 8; kk++) {
+            // 8 keys = two 4-row groups (SBO = 512 B); 32-column chunks LBO apart
+            const uint64_t bdesc =
+                smem_desc(vbase + kk * 1024, VK * 128, 512, kLayoutSw128Base32);
+            mma_ts(t_o, t_s(b) + h * VK + kk * 8, bdesc, idesc_pv,
+                   (jj > 0 || h > 0 || kk > 0) ? 1u : 0u);
+          }
+          tc_commit(bar_v_empty(sv));
         }
-        tc_commit(bar_v_empty(s));
         tc_commit(bar_o_done);
         return true;
       };
       for (int j = 0; j < n_kv && ok; j++) {
-        const int s = j % NS, b = j & 1;
-        ok = mbar_wait(bar_k_full(s), (j / NS) & 1, abort_flag, p.err);
+        const int s = j % NKS, b = j & 1;
+        ok = mbar_wait(bar_k_full(s), (j / NKS) & 1, abort_flag, p.err);
         if (!ok) break;
         tc_fence_after();
-        const uint32_t kbase = sK + s * C::kKVBytes;
+        const uint32_t kbase = sK + s * C::kKBytes;
 #pragma unroll
         for (int kk = 0; kk < D / 8; kk++) {
-          const uint32_t off = (kk >> 2) * 0u + (kk & 3) * 32;
-          const uint64_t adesc = smem_desc(sQ + (kk >> 2) * kBM * 128 + off, 16, 1024);
-          const uint64_t bdesc = smem_desc(kbase + (kk >> 2) * BK * 128 + off, 16, 1024);
-          mma_ss(t_s(b), adesc, bdesc, idesc_qk, kk > 0 ? 1u : 0u);
+          const uint64_t bdesc =
+              smem_desc(kbase + (kk >> 2) * BK * 128 + (kk & 3) * 32, 16, 1024, kLayoutSw128);
+          mma_ts(t_s(b), t_q + kk * 8, bdesc, idesc_qk, kk > 0 ? 1u : 0u);
         }
         tc_commit(bar_s_full(b));
         tc_commit(bar_k_empty(s));
         if (j > 0) ok = issue_pv(j - 1);
       }
-      if (ok && n_kv > 0) issue_pv(n_kv - 1);
+      if (ok && n_kv > 0 && issue_pv(n_kv - 1)) tc_commit(bar_o_final);
       // Drain: all MMAs issued by this thread complete before TMEM is freed.
       tc_commit(bar_drain);
       volatile int no_abort = 0;
@@ -359,34 +403,66 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int r = quarter * 32 + lane;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const long long qg = p.q_offset + q0 + r;
+    const float c_log2 = p.scale_log2;
+    bool ok = !skip;
+    // Stage this row of Q into TMEM, rounded to TF32 (round-to-nearest).
+    if (ok) {
+      const bool valid = r < q_rows;
+      const float4* qrow = reinterpret_cast<const float4*>(p.q + ((size_t)bh * p.sq + q0 + r) * D);
+#pragma unroll
+      for (int c = 0; c < D / 32; c++) {
+        uint32_t rr[32];
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+          const float4 v4 = valid ? __ldg(qrow + c * 8 + e) : make_float4(0.f, 0.f, 0.f, 0.f);
+          rr[4 * e + 0] = to_tf32_rna(v4.x);
+          rr[4 * e + 1] = to_tf32_rna(v4.y);
+          rr[4 * e + 2] = to_tf32_rna(v4.z);
+          rr[4 * e + 3] = to_tf32_rna(v4.w);
+        }
+        tmem_st32(t_q + lane_off + c * 32, rr);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(bar_q_full);
+    }
     float m = -INFINITY;  // running max in log2 units (possibly stale by < 2^8)
     float l = 0.0f;
-    bool ok = !skip;
     for (int j = 0; j < n_kv && ok; j++) {
       const int b = j & 1;
       ok = __all_sync(0xffffffffu, mbar_wait(bar_s_full(b), (j >> 1) & 1, abort_flag, p.err));
       if (!ok) break;
       tc_fence_after();
       float x[BK];
+      {
+        uint32_t sr[BK];
 #pragma unroll
-      for (int c = 0; c < BK / 32; c++) {
-        uint32_t rr[32];
-        tmem_ld32(t_s(b) + lane_off + c * 32, rr);
-        tmem_wait_ld();
+        for (int c = 0; c < BK / 32; c++)
+          tmem_ld32(t_s(b) + lane_off + c * 32, *reinterpret_cast<uint32_t(*)[32]>(sr + c * 32));
+        tmem_wait_ld_regs(sr);
 #pragma unroll
-        for (int e = 0; e < 32; e++) x[c * 32 + e] = __uint_as_float(rr[e]);
+        for (int e = 0; e < BK; e++) x[e] = __uint_as_float(sr[e]);
       }
-      // visible keys of this row in tile j: [0, lim)
+      // visible keys of this row in tile j: [0, lim); mask only partial tiles
       const int kbase = j * BK;
       int lim = min(BK, p.sk - kbase);
       if (p.causal) lim = min(lim, causal_limit(qg, p.k_offset + kbase, BK));
-      float mx = -INFINITY;
+      if (!__all_sync(0xffffffffu, lim == BK)) {
 #pragma unroll
-      for (int e = 0; e < BK; e++) {
-        x[e] = (e < lim) ? x[e] * p.scale_log2 : -INFINITY;
-        mx = fmaxf(mx, x[e]);
+        for (int e = 0; e < BK; e++) x[e] = (e < lim) ? x[e] : -INFINITY;
       }
-      const float m_new = fmaxf(m, mx);
+      float mx[4];
+#pragma unroll
+      for (int t = 0; t < 4; t++) mx[t] = -INFINITY;
+#pragma unroll
+      for (int e = 0; e < BK; e += 8) {
+        const int t = (e >> 3) & 3;
+        mx[t] = fmax3(mx[t], x[e], x[e + 1]);
+        mx[t] = fmax3(mx[t], x[e + 2], x[e + 3]);
+        mx[t] = fmax3(mx[t], x[e + 4], x[e + 5]);
+        mx[t] = fmax3(mx[t], x[e + 6], x[e + 7]);
+      }
+      const float m_new = fmaxf(m, fmax3(mx[0], mx[1], fmaxf(mx[2], mx[3])) * c_log2);
       float corr = 1.0f;
       bool need = false;
       if (m == -INFINITY) {
@@ -405,35 +481,36 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int c = 0; c < D / 32; c++) {
           uint32_t rr[32];
           tmem_ld32(t_o + lane_off + c * 32, rr);
-          tmem_wait_ld();
+          tmem_wait_ld_regs(rr);
 #pragma unroll
           for (int e = 0; e < 32; e++) rr[e] = __float_as_uint(__uint_as_float(rr[e]) * corr);
           tmem_st32(t_o + lane_off + c * 32, rr);
         }
         l *= corr;
       }
-      const bool any_visible = (m != -INFINITY);
-      float rowsum = 0.0f;
+      // p = 2^(s*scale*log2e - m), truncated to TF32 exactly as the tensor core
+      // reads it, so the row sum l matches the P the PV MMA multiplies.
+      const float neg_m = (m == -INFINITY) ? 0.0f : -m;
+      float rs[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int c = 0; c < BK / 32; c++) {
         uint32_t rr[32];
 #pragma unroll
         for (int e = 0; e < 32; e++) {
-          float pe = any_visible ? ex2(x[c * 32 + e] - m) : 0.0f;
-          uint32_t t = to_tf32_rna(pe);
-          rowsum += __uint_as_float(t);
+          const uint32_t t = __float_as_uint(ex2(fmaf(x[c * 32 + e], c_log2, neg_m))) & 0xFFFFE000u;
+          rs[e & 3] += __uint_as_float(t);
           rr[e] = t;
         }
         tmem_st32(t_s(b) + lane_off + c * 32, rr);
       }
-      l += rowsum;
+      l += (rs[0] + rs[1]) + (rs[2] + rs[3]);
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(bar_p_full(b));
     }
     // epilogue: out = O / l, lse = ln(sum exp(s)) = (m + log2 l) * ln 2
     if (n_kv > 0) {
-      const bool w = ok ? mbar_wait(bar_o_done, (n_kv - 1) & 1, abort_flag, p.err) : false;
+      const bool w = ok ? mbar_wait(bar_o_final, 0, abort_flag, p.err) : false;
       ok = __all_sync(0xffffffffu, w);
     }
     if (ok) {
@@ -446,7 +523,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t rr[32];
         if (n_kv > 0) {
           tmem_ld32(t_o + lane_off + c * 32, rr);
-          tmem_wait_ld();
+          tmem_wait_ld_regs(rr);
         } else {
 #pragma unroll
           for (int e = 0; e < 32; e++) rr[e] = 0u;
@@ -491,8 +568,9 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
   return fn;
 }
 
-// 3-D map over [bh][seq][d] f32, box = 32 f32 x rows x 1, 128-byte swizzle.
-bool make_map(CUtensorMap* map, const float* base, int d, int seq, int bh, int rows) {
+// 3-D map over [bh][seq][d] f32, box = 32 f32 x rows x 1.
+bool make_map(CUtensorMap* map, const float* base, int d, int seq, int bh, int rows,
+              CUtensorMapSwizzle swizzle) {
   auto fn = get_encode_fn();
   if (!fn) return false;
   cuuint64_t dims[3] = {(cuuint64_t)d, (cuuint64_t)seq, (cuuint64_t)bh};
@@ -500,25 +578,25 @@ bool make_map(CUtensorMap* map, const float* base, int d, int seq, int bh, int r
   cuuint32_t box[3] = {32, (cuuint32_t)rows, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims,
-                  strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
 
-template <int D, int BK, int NS>
+template <int D, int BK, int VK, int NKS, int NVS>
 cudaError_t launch_tf32(const FwdParams& p, cudaStream_t s) {
-  using C = TcCfg<D, BK, NS>;
-  CUtensorMap mq, mk, mv;
-  if (!make_map(&mq, p.q, D, p.sq, p.bh, kBM) || !make_map(&mk, p.k, D, p.sk, p.bh, BK) ||
-      !make_map(&mv, p.v, D, p.sk, p.bh, BK))
+  using C = TcCfg<D, BK, VK, NKS, NVS>;
+  CUtensorMap mk, mv;
+  if (!make_map(&mk, p.k, D, p.sk, p.bh, BK, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !make_map(&mv, p.v, D, p.sk, p.bh, VK, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B))
     return cudaErrorInvalidValue;
   static std::atomic<unsigned long long> attr_set{0};  // one bit per device
   int dev = 0;
   cudaGetDevice(&dev);
   const unsigned long long bit = 1ull << (dev & 63);
   if (!(attr_set.load() & bit)) {
-    cudaError_t e = cudaFuncSetAttribute(tc_fwd_tf32<D, BK, NS>,
+    cudaError_t e = cudaFuncSetAttribute(tc_fwd_tf32<D, BK, VK, NKS, NVS>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          C::kSmemBytes);
     if (e != cudaSuccess) return e;
@@ -526,7 +604,7 @@ cudaError_t launch_tf32(const FwdParams& p, cudaStream_t s) {
   }
   const int n_qt = (p.sq + kBM - 1) / kBM;
   dim3 grid(p.bh, n_qt);
-  tc_fwd_tf32<D, BK, NS><<<grid, kThreads, C::kSmemBytes, s>>>(mq, mk, mv, p);
+  tc_fwd_tf32<D, BK, VK, NKS, NVS><<<grid, kThreads, C::kSmemBytes, s>>>(mk, mv, p);
   count_launch();
   return cudaGetLastError();
 }
@@ -542,8 +620,8 @@ size_t tc_scratch_floats(const FwdParams&, int) { return 0; }
 cudaError_t launch_tc(const FwdParams& p, int precision, float*, size_t, cudaStream_t s) {
   if (precision != 0) return cudaErrorInvalidValue;
   if (p.sq > 65535 * kBM) return cudaErrorInvalidValue;
-  if (p.d == 128) return launch_tf32<128, 64, 2>(p, s);
-  if (p.d == 64) return launch_tf32<64, 128, 2>(p, s);
+  if (p.d == 128) return launch_tf32<128, 128, 64, 2, 3>(p, s);
+  if (p.d == 64) return launch_tf32<64, 128, 128, 3, 3>(p, s);
   return cudaErrorInvalidValue;
 }
 
