@@ -222,6 +222,32 @@ __host__ __device__ constexpr uint32_t instr_desc(int M, int N, bool b_mn_major)
          ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
+// ---- optional cycle trace (diagnostic builds only, -DFA_TRACE) -------------
+#ifdef FA_TRACE
+__device__ unsigned long long g_fa_trace[32];
+#define FA_TR_T0() long long tr_t0 = clock64()
+#define FA_TR_ADD(slot) atomicAdd(&g_fa_trace[slot], (unsigned long long)(clock64() - tr_t0))
+#define FA_TR_CNT(slot) atomicAdd(&g_fa_trace[slot], 1ull)
+// per-tile event timestamps of one CTA pair (blockIdx.y == 0, blockIdx.z == 0)
+__device__ long long g_fa_events[12][256];
+#define FA_EV(kind, j)                                                              \
+  if (blockIdx.y == 0 && blockIdx.z == 0 && blockIdx.x == 0 && (j) < 256)           \
+  g_fa_events[kind][j] = clock64()
+#else
+#define FA_EV(kind, j) \
+  do {                 \
+  } while (0)
+#define FA_TR_T0() \
+  do {             \
+  } while (0)
+#define FA_TR_ADD(slot) \
+  do {                  \
+  } while (0)
+#define FA_TR_CNT(slot) \
+  do {                  \
+  } while (0)
+#endif
+
 // ---- the kernel ------------------------------------------------------------
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
   float r;
@@ -262,6 +288,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kOffBar + C::kNumBars * 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
+#ifdef FA_TRACE
+  const long long tr_kstart = clock64();
+#endif
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int bh = blockIdx.x;
   const int n_qt = gridDim.y;
@@ -310,39 +339,55 @@ __global__ void __launch_bounds__(kThreads, 1)
   const bool skip = *abort_flag != 0;
 
   if (warp == 0) {
-    // ------------------------------ TMA producer (K and V rings)
+    // ------------------------------ TMA producer, K ring
+    // K and V have separate producers so a K load never waits behind a V slot
+    // (V slots free only after PV, K slots right after QK^T).
     if (lane == 0 && !skip) {
-      int issued_k = 0, issued_v = 0;
+      int issued = 0;
       bool ok = true;
       for (int j = 0; j < n_kv && ok; j++) {
         const int sk = j % NKS;
-        if (j >= NKS) ok = mbar_wait(bar_k_empty(sk), ((j / NKS) & 1) ^ 1, abort_flag, p.err);
+        {
+          FA_TR_T0();
+          if (j >= NKS) ok = mbar_wait(bar_k_empty(sk), ((j / NKS) & 1) ^ 1, abort_flag, p.err);
+          FA_TR_ADD(0);
+        }
         if (!ok) break;
         mbar_expect_tx(bar_k_full(sk), C::kKBytes);
         for (int c = 0; c < C::kChunks; c++)
           tma_load_3d(sK + sk * C::kKBytes + c * BK * 128, &tmK, bar_k_full(sk), 32 * c, j * BK, bh);
-        issued_k = j + 1;
-        for (int h = 0; h < VS && ok; h++) {
-          const int g = j * VS + h, sv = g % NVS;
+        issued = j + 1;
+      }
+      // Wait (bounded, ignoring the abort flag) for the last load of every
+      // slot, so no TMA write can land after the CTA exits even when a
+      // consumer role aborted.  On the normal path these have all completed.
+      volatile int no_abort = 0;
+      for (int j = max(0, issued - NKS); j < issued; j++)
+        mbar_wait(bar_k_full(j % NKS), (j / NKS) & 1, &no_abort, p.err);
+    }
+    __syncwarp();
+  } else if (warp == 2) {
+    // ------------------------------ TMA producer, V ring (VK-key sub-tiles)
+    if (lane == 0 && !skip) {
+      int issued = 0;
+      bool ok = true;
+      const int n_v = n_kv * VS;
+      for (int g = 0; g < n_v && ok; g++) {
+        const int sv = g % NVS;
+        {
+          FA_TR_T0();
           if (g >= NVS) ok = mbar_wait(bar_v_empty(sv), ((g / NVS) & 1) ^ 1, abort_flag, p.err);
-          if (!ok) break;
-          mbar_expect_tx(bar_v_full(sv), C::kVBytes);
-          for (int c = 0; c < C::kChunks; c++)
-            tma_load_3d(sV + sv * C::kVBytes + c * VK * 128, &tmV, bar_v_full(sv), 32 * c, g * VK,
-                        bh);
-          issued_v = g + 1;
+          FA_TR_ADD(1);
         }
+        if (!ok) break;
+        mbar_expect_tx(bar_v_full(sv), C::kVBytes);
+        for (int c = 0; c < C::kChunks; c++)
+          tma_load_3d(sV + sv * C::kVBytes + c * VK * 128, &tmV, bar_v_full(sv), 32 * c, g * VK, bh);
+        issued = g + 1;
       }
-      {
-        // Wait (bounded, ignoring the abort flag) for the last load of every
-        // slot, so no TMA write can land after the CTA exits even when a
-        // consumer role aborted.  On the normal path these have all completed.
-        volatile int no_abort = 0;
-        for (int j = max(0, issued_k - NKS); j < issued_k; j++)
-          mbar_wait(bar_k_full(j % NKS), (j / NKS) & 1, &no_abort, p.err);
-        for (int g = max(0, issued_v - NVS); g < issued_v; g++)
-          mbar_wait(bar_v_full(g % NVS), (g / NVS) & 1, &no_abort, p.err);
-      }
+      volatile int no_abort = 0;
+      for (int g = max(0, issued - NVS); g < issued; g++)
+        mbar_wait(bar_v_full(g % NVS), (g / NVS) & 1, &no_abort, p.err);
     }
     __syncwarp();
   } else if (warp == 1) {
@@ -354,11 +399,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       auto issue_pv = [&](int jj) -> bool {
         const int b = jj & 1;
-        if (!mbar_wait(bar_p_full(b), (jj >> 1) & 1, abort_flag, p.err)) return false;
+        {
+          FA_TR_T0();
+          if (!mbar_wait(bar_p_full(b), (jj >> 1) & 1, abort_flag, p.err)) return false;
+          FA_TR_ADD(3);
+        }
 #pragma unroll
         for (int h = 0; h < VS; h++) {
           const int g = jj * VS + h, sv = g % NVS;
-          if (!mbar_wait(bar_v_full(sv), (g / NVS) & 1, abort_flag, p.err)) return false;
+          {
+            FA_TR_T0();
+            if (!mbar_wait(bar_v_full(sv), (g / NVS) & 1, abort_flag, p.err)) return false;
+            FA_TR_ADD(4);
+          }
           tc_fence_after();
           const uint32_t vbase = sV + sv * C::kVBytes;
 #pragma unroll
@@ -376,7 +429,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       };
       for (int j = 0; j < n_kv && ok; j++) {
         const int s = j % NKS, b = j & 1;
-        ok = mbar_wait(bar_k_full(s), (j / NKS) & 1, abort_flag, p.err);
+        {
+          FA_TR_T0();
+          ok = mbar_wait(bar_k_full(s), (j / NKS) & 1, abort_flag, p.err);
+          FA_TR_ADD(2);
+        }
         if (!ok) break;
         tc_fence_after();
         const uint32_t kbase = sK + s * C::kKBytes;
@@ -430,8 +487,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     float l = 0.0f;
     for (int j = 0; j < n_kv && ok; j++) {
       const int b = j & 1;
-      ok = __all_sync(0xffffffffu, mbar_wait(bar_s_full(b), (j >> 1) & 1, abort_flag, p.err));
+      {
+        FA_TR_T0();
+        ok = __all_sync(0xffffffffu, mbar_wait(bar_s_full(b), (j >> 1) & 1, abort_flag, p.err));
+        if (threadIdx.x == 128) FA_TR_ADD(5);
+      }
       if (!ok) break;
+      FA_TR_T0();
       tc_fence_after();
       float x[BK];
       {
@@ -473,6 +535,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         m = m_new;
       }
       if (__any_sync(0xffffffffu, need)) {
+        if (threadIdx.x == 128) FA_TR_CNT(7);
         // O is being accumulated by PV_{j-1}: wait for it, then rescale in TMEM.
         ok = __all_sync(0xffffffffu, mbar_wait(bar_o_done, (j - 1) & 1, abort_flag, p.err));
         if (!ok) break;
@@ -507,6 +570,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(bar_p_full(b));
+      if (threadIdx.x == 128) {
+        FA_TR_ADD(6);
+        FA_TR_CNT(8);
+      }
     }
     // epilogue: out = O / l, lse = ln(sum exp(s)) = (m + log2 l) * ln 2
     if (n_kv > 0) {
@@ -545,9 +612,583 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_before();
   }
   __syncthreads();
+#ifdef FA_TRACE
+  if (threadIdx.x == 0) {
+    atomicAdd(&g_fa_trace[9], (unsigned long long)(clock64() - tr_kstart));
+    atomicAdd(&g_fa_trace[10], 1ull);
+  }
+#endif
   if (warp == 1) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"((uint32_t)C::kTmemCols)
+                 : "memory");
+  }
+}
+
+// ===========================================================================
+// 2-SM pair kernel (cta_group::2).  A cluster of two CTAs on two SMs computes
+// 256 query rows (128 per CTA) of one (batch, head) slice.  The leader CTA
+// (cluster rank 0) issues every MMA for the pair with M = 256: each SM's tensor
+// core computes its own 128 rows, reading the B operand halves from both SMs'
+// shared memory.  Each CTA therefore loads only half of every K tile (64 of
+// its 128 keys) and half of every V tile (64 of the 128 head columns), which
+// halves the L2->SM traffic per FLOP and doubles how many tiles the same
+// shared memory can keep in flight.  No load is multicast: each CTA's TMA
+// writes only its own shared memory and signals the leader's barrier.
+//
+// Per CTA: TMEM columns Q [0, D), O [D, 2D), S/P buffers [2D, 2D + 2*BK);
+// shared memory: K half-tiles [D/32 chunks][BK/2 keys][32], V half-tiles
+// [D/64 chunks][BK keys][32] (the CTA's d range rank*D/2 .. +D/2).
+// Barriers live at the same offsets in both CTAs.  q_full, k_full, v_full and
+// p_full are waited on only in the leader (the peer arrives on them remotely);
+// the MMA completions are committed to both CTAs' copies of k_empty, v_empty,
+// s_full, o_done, o_final and drain.
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t map_to_rank(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+// Arrive on a barrier of the peer CTA.  Default semantics (release at CTA
+// scope): every use follows a tcgen05.wait::st, so the TMEM data it publishes
+// is already complete; a cluster-scope release costs ~1000 cycles per arrive.
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_bar) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx_cluster(uint32_t cluster_bar, uint32_t bytes) {
+  asm volatile(
+      "mbarrier.arrive.expect_tx.release.cluster.shared::cluster.b64 _, [%0], %1;" ::"r"(
+          cluster_bar),
+      "r"(bytes)
+      : "memory");
+}
+// TMA tile load into this CTA's shared memory, completing on a barrier that may
+// live in the peer CTA of the pair.
+__device__ __forceinline__ void tma_load_3d_pair(uint32_t dst, const CUtensorMap* map,
+                                                 uint32_t cluster_bar, int x, int y, int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.tile.mbarrier::complete_tx::"
+      "bytes [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(cluster_bar), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+__device__ __forceinline__ void tc_commit_pair(uint32_t cluster_bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          cluster_bar)
+      : "memory");
+}
+__device__ __forceinline__ void mma_ts_pair(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                            uint32_t idesc, uint32_t accum) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accum)
+      : "memory");
+}
+// Warp-wide forms: every lane executes them with uniform operands and one
+// elected lane issues the instruction.
+__device__ __forceinline__ void mma_ts_pair_elect(uint32_t d_tmem, uint32_t a_tmem,
+                                                  uint64_t b_desc, uint32_t idesc,
+                                                  uint32_t accum) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "@e tcgen05.mma.cta_group::2.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accum)
+      : "memory");
+}
+__device__ __forceinline__ void tc_commit_pair_elect(uint32_t cluster_bar) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(
+          cluster_bar)
+      : "memory");
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                   : "memory");
+}
+
+// Named barrier over `n` threads that also ORs a per-thread flag: every
+// participant gets the same result, so a failure seen by any of them makes all
+// of them leave a loop together (a plain bar.sync would leave the others
+// waiting forever).
+__device__ __forceinline__ bool bar_any(uint32_t id, uint32_t n, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred pi, po;\n\t"
+      "setp.ne.u32 pi, %1, 0;\n\t"
+      "bar.red.or.pred po, %2, %3, pi;\n\t"
+      "selp.u32 %0, 1, 0, po;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)v), "r"(id), "r"(n)
+      : "memory");
+  return r != 0;
+}
+
+template <int D, int BK, int NKS, int NVS>
+struct PairCfg {
+  static constexpr int kKHalf = BK / 2;                 // keys of a K tile held per CTA
+  static constexpr int kDHalf = D / 2;                  // head columns of a V tile per CTA
+  static constexpr int kKBytes = kKHalf * D * 4;        // per CTA
+  static constexpr int kVBytes = BK * kDHalf * 4;       // per CTA
+  static constexpr int kOffK = 0;
+  static constexpr int kOffV = NKS * kKBytes;
+  static constexpr int kOffBar = kOffV + NVS * kVBytes;
+  static constexpr int kNumBars = 1 + 2 * NKS + 2 * NVS + 2 + 2 + 3;
+  static constexpr int kOffRed = (kOffBar + kNumBars * 8 + 16 + 15) / 16 * 16;
+  static constexpr int kSmemBytes = kOffRed + 3 * 2 * 128 * 4 + 1024;
+  static constexpr int kTmemColsUsed = 2 * D + 2 * BK;
+  static constexpr int kTmemCols = kTmemColsUsed <= 256 ? 256 : 512;
+  static_assert(D % 64 == 0 && D <= 128, "pair kernel: D in {64, 128}");
+  static_assert(BK % 64 == 0 && BK <= 256, "pair kernel: BK multiple of 64");
+  static_assert(kTmemColsUsed <= 512, "TMEM budget");
+  static_assert(kSmemBytes <= 232448, "shared-memory budget");
+};
+
+constexpr int kThreadsPair = 384;  // 12 warps: 2 producers, MMA, idle, 2 softmax warpgroups
+
+template <int D, int BK, int NKS, int NVS>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPair, 1)
+    tc_fwd_tf32_pair(const __grid_constant__ CUtensorMap tmK,
+                     const __grid_constant__ CUtensorMap tmV, FwdParams p) {
+  using C = PairCfg<D, BK, NKS, NVS>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+#ifdef FA_TRACE
+  const long long tr_kstart = clock64();
+#endif
+  const uint32_t rank = cluster_rank();
+  const bool leader = rank == 0;
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t sK = sbase + C::kOffK;
+  const uint32_t sV = sbase + C::kOffV;
+  const uint32_t bar0 = sbase + C::kOffBar;
+  const uint32_t bar_q_full = bar0;
+  auto bar_k_full = [&](int s) { return bar0 + 8u * (1 + s); };
+  auto bar_k_empty = [&](int s) { return bar0 + 8u * (1 + NKS + s); };
+  auto bar_v_full = [&](int s) { return bar0 + 8u * (1 + 2 * NKS + s); };
+  auto bar_v_empty = [&](int s) { return bar0 + 8u * (1 + 2 * NKS + NVS + s); };
+  constexpr uint32_t kB2 = 1 + 2 * NKS + 2 * NVS;
+  auto bar_s_full = [&](int b) { return bar0 + 8u * (kB2 + b); };
+  auto bar_p_full = [&](int b) { return bar0 + 8u * (kB2 + 2 + b); };
+  const uint32_t bar_o_done = bar0 + 8u * (kB2 + 4);
+  const uint32_t bar_drain = bar0 + 8u * (kB2 + 5);
+  const uint32_t bar_o_final = bar0 + 8u * (kB2 + 6);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kOffBar + C::kNumBars * 8);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  // the same barrier in the leader's / the peer's shared memory (cluster addresses)
+  auto at_leader = [&](uint32_t bar) { return map_to_rank(bar, 0); };
+  auto at_peer = [&](uint32_t bar) { return map_to_rank(bar, 1); };
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int bh = blockIdx.y;
+  const int n_pairs = gridDim.z;
+  const int pair = n_pairs - 1 - (int)blockIdx.z;  // heaviest causal pairs dispatched first
+  const int q0_pair = pair * 2 * kBM;
+  const int q0 = q0_pair + (int)rank * kBM;        // this CTA's first row
+  const int q_rows = max(0, min(kBM, p.sq - q0));
+  const int pair_rows = min(2 * kBM, p.sq - q0_pair);
+  int kend = p.sk;
+  if (p.causal) kend = causal_limit(p.q_offset + q0_pair + pair_rows - 1, p.k_offset, p.sk);
+  const int n_kv = (kend + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    mbar_init(bar_q_full, 16);  // 8 softmax warps x 2 CTAs
+    for (int s = 0; s < NKS; s++) {
+      mbar_init(bar_k_full(s), 2);
+      mbar_init(bar_k_empty(s), 1);
+    }
+    for (int s = 0; s < NVS; s++) {
+      mbar_init(bar_v_full(s), 2);
+      mbar_init(bar_v_empty(s), 1);
+    }
+    for (int b = 0; b < 2; b++) {
+      mbar_init(bar_s_full(b), 1);
+      mbar_init(bar_p_full(b), 16);
+    }
+    mbar_init(bar_o_done, 1);
+    mbar_init(bar_drain, 1);
+    mbar_init(bar_o_final, 1);
+    *abort_flag = (*(volatile int*)p.err != 0) ? 1 : 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"((uint32_t)C::kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  cluster_sync_all();  // barriers of both CTAs initialised before any remote arrive
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t t_q = tmem;
+  const uint32_t t_o = tmem + (uint32_t)D;
+  auto t_s = [&](int b) { return tmem + (uint32_t)(2 * D + b * BK); };
+  // Either CTA's earlier failure skips the work of both (the flag is global).
+  const bool skip = *abort_flag != 0;
+
+  if (warp == 0) {
+    // ------------------------------ K producer: this CTA's 64-key half of each tile
+    if (lane == 0 && !skip) {
+      int issued = 0;
+      bool ok = true;
+      for (int j = 0; j < n_kv && ok; j++) {
+        const int sk = j % NKS;
+        {
+          FA_TR_T0();
+          if (j >= NKS) ok = mbar_wait(bar_k_empty(sk), ((j / NKS) & 1) ^ 1, abort_flag, p.err);
+          if (leader) FA_TR_ADD(0);
+        }
+        if (!ok) break;
+        FA_EV(8, j);
+        const uint32_t full = at_leader(bar_k_full(sk));
+        mbar_expect_tx_cluster(full, C::kKBytes);
+        for (int c = 0; c < D / 32; c++)
+          tma_load_3d_pair(sK + sk * C::kKBytes + c * C::kKHalf * 128, &tmK, full, 32 * c,
+                           j * BK + (int)rank * C::kKHalf, bh);
+        issued = j + 1;
+      }
+      volatile int no_abort = 0;
+      if (leader)
+        for (int j = max(0, issued - NKS); j < issued; j++)
+          mbar_wait(bar_k_full(j % NKS), (j / NKS) & 1, &no_abort, p.err);
+    }
+    __syncwarp();
+  } else if (warp == 2) {
+    // ------------------------------ V producer: all BK keys x this CTA's D/2 columns
+    if (lane == 0 && !skip) {
+      int issued = 0;
+      bool ok = true;
+      for (int j = 0; j < n_kv && ok; j++) {
+        const int sv = j % NVS;
+        {
+          FA_TR_T0();
+          if (j >= NVS) ok = mbar_wait(bar_v_empty(sv), ((j / NVS) & 1) ^ 1, abort_flag, p.err);
+          if (leader) FA_TR_ADD(1);
+        }
+        if (!ok) break;
+        FA_EV(9, j);
+        const uint32_t full = at_leader(bar_v_full(sv));
+        mbar_expect_tx_cluster(full, C::kVBytes);
+        for (int c = 0; c < C::kDHalf / 32; c++)
+          tma_load_3d_pair(sV + sv * C::kVBytes + c * BK * 128, &tmV, full,
+                           (int)rank * C::kDHalf + 32 * c, j * BK, bh);
+        issued = j + 1;
+      }
+      volatile int no_abort = 0;
+      if (leader)
+        for (int j = max(0, issued - NVS); j < issued; j++)
+          mbar_wait(bar_v_full(j % NVS), (j / NVS) & 1, &no_abort, p.err);
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------ MMA issuer (leader CTA only)
+    // The whole warp runs this loop so descriptors and addresses stay
+    // warp-uniform (uniform registers); one elected lane issues each
+    // tcgen05.mma / tcgen05.commit.
+    if (leader && !skip) {
+      constexpr uint32_t idesc_qk = instr_desc(2 * kBM, BK, false);
+      constexpr uint32_t idesc_pv = instr_desc(2 * kBM, D, true);
+      auto commit_both = [&](uint32_t bar) {
+        tc_commit_pair_elect(bar);           // this CTA's copy
+        tc_commit_pair_elect(at_peer(bar));  // the peer's copy
+      };
+      bool ok = __all_sync(0xffffffffu, mbar_wait(bar_q_full, 0, abort_flag, p.err));
+      tc_fence_after();
+      auto issue_pv = [&](int jj) -> bool {
+        const int b = jj & 1, sv = jj % NVS;
+        {
+          FA_TR_T0();
+          if (!__all_sync(0xffffffffu, mbar_wait(bar_p_full(b), (jj >> 1) & 1, abort_flag, p.err)))
+            return false;
+          if (lane == 0) FA_TR_ADD(3);
+          FA_EV(2, jj);
+        }
+        {
+          FA_TR_T0();
+          if (!__all_sync(0xffffffffu, mbar_wait(bar_v_full(sv), (jj / NVS) & 1, abort_flag, p.err)))
+            return false;
+          if (lane == 0) FA_TR_ADD(4);
+          FA_EV(10, jj);
+        }
+        tc_fence_after();
+        // 8 keys per MMA = two 4-row groups (SBO = 512 B); 32-column chunks LBO apart
+        const uint64_t vdesc = smem_desc(sV + sv * C::kVBytes, BK * 128, 512, kLayoutSw128Base32);
+#pragma unroll
+        for (int kk = 0; kk < BK / 8; kk++)
+          mma_ts_pair_elect(t_o, t_s(b) + kk * 8, vdesc + (uint64_t)(kk * 64), idesc_pv,
+                            (jj > 0 || kk > 0) ? 1u : 0u);
+        commit_both(bar_v_empty(sv));
+        commit_both(bar_o_done);
+        FA_EV(3, jj);
+        return true;
+      };
+      for (int j = 0; j < n_kv && ok; j++) {
+        const int s = j % NKS, b = j & 1;
+        {
+          FA_TR_T0();
+          ok = __all_sync(0xffffffffu, mbar_wait(bar_k_full(s), (j / NKS) & 1, abort_flag, p.err));
+          if (lane == 0) FA_TR_ADD(2);
+          FA_EV(0, j);
+        }
+        if (!ok) break;
+        tc_fence_after();
+        const uint64_t kdesc = smem_desc(sK + s * C::kKBytes, 16, 1024, kLayoutSw128);
+#pragma unroll
+        for (int kk = 0; kk < D / 8; kk++)
+          mma_ts_pair_elect(t_s(b), t_q + kk * 8,
+                            kdesc + (uint64_t)(((kk >> 2) * C::kKHalf * 128 + (kk & 3) * 32) >> 4),
+                            idesc_qk, kk > 0 ? 1u : 0u);
+        commit_both(bar_s_full(b));
+        commit_both(bar_k_empty(s));
+        FA_EV(1, j);
+        if (j > 0) ok = issue_pv(j - 1);
+      }
+      if (ok && n_kv > 0 && issue_pv(n_kv - 1)) commit_both(bar_o_final);
+      commit_both(bar_drain);
+    }
+    __syncwarp();
+  } else if (warp >= kSoftmaxWarp0) {
+    // ------------------------------ softmax: two warpgroups, thread = (row, half)
+    // Warpgroup g (warps 4-7: g = 0, warps 8-11: g = 1) handles columns
+    // [g*BK/2, (g+1)*BK/2) of every score row and O columns [g*D/2, (g+1)*D/2):
+    // two warps per scheduler hide each other's latency.  The two halves of a
+    // row exchange their partial maxima once per tile through shared memory;
+    // each keeps its own partial row sum until the epilogue.
+    constexpr int HC = BK / 2, HD = D / 2;
+    const int g = (warp - kSoftmaxWarp0) >> 2;
+    const int quarter = warp & 3;  // TMEM lanes 32*quarter..
+    const int r = quarter * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const long long qg = p.q_offset + q0 + r;
+    const float c_log2 = p.scale_log2;
+    float* red = reinterpret_cast<float*>(smem + C::kOffRed);  // [3][2][128]
+    bool ok = !skip;
+    auto warp_arrive_leader = [&](uint32_t bar) {
+      __syncwarp();
+      if (lane == 0) {
+        if (leader)
+          mbar_arrive(bar);
+        else
+          mbar_arrive_remote(at_leader(bar));
+      }
+    };
+    if (ok) {
+      const bool valid = r < q_rows;
+      const float4* qrow =
+          reinterpret_cast<const float4*>(p.q + ((size_t)bh * p.sq + q0 + r) * D + g * HD);
+#pragma unroll
+      for (int c = 0; c < HD / 32; c++) {
+        uint32_t rr[32];
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+          const float4 v4 = valid ? __ldg(qrow + c * 8 + e) : make_float4(0.f, 0.f, 0.f, 0.f);
+          rr[4 * e + 0] = to_tf32_rna(v4.x);
+          rr[4 * e + 1] = to_tf32_rna(v4.y);
+          rr[4 * e + 2] = to_tf32_rna(v4.z);
+          rr[4 * e + 3] = to_tf32_rna(v4.w);
+        }
+        tmem_st32(t_q + lane_off + g * HD + c * 32, rr);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      warp_arrive_leader(bar_q_full);
+    }
+    float m = -INFINITY, l = 0.0f;  // l: this half's partial row sum
+    for (int j = 0; j < n_kv && ok; j++) {
+      const int b = j & 1;
+      bool w;
+      {
+        FA_TR_T0();
+        w = __all_sync(0xffffffffu, mbar_wait(bar_s_full(b), (j >> 1) & 1, abort_flag, p.err));
+        if (threadIdx.x == 128 && leader) FA_TR_ADD(5);
+        if (threadIdx.x == 128) FA_EV(4, j);
+        if (threadIdx.x == 256) FA_EV(6, j);
+      }
+      FA_TR_T0();
+      tc_fence_after();
+      float x[HC];
+#ifdef FA_TRACE
+      long long tr_a = clock64();
+#endif
+      if (w) {
+        uint32_t sr[HC];
+#pragma unroll
+        for (int c = 0; c < HC / 32; c++)
+          tmem_ld32(t_s(b) + lane_off + g * HC + c * 32,
+                    *reinterpret_cast<uint32_t(*)[32]>(sr + c * 32));
+        tmem_wait_ld_regs(sr);
+#ifdef FA_TRACE
+        if (threadIdx.x == 128 && leader) atomicAdd(&g_fa_trace[11], (unsigned long long)(clock64() - tr_a));
+        tr_a = clock64();
+#endif
+#pragma unroll
+        for (int e = 0; e < HC; e++) x[e] = __uint_as_float(sr[e]);
+      } else {
+#pragma unroll
+        for (int e = 0; e < HC; e++) x[e] = -INFINITY;
+      }
+      const int kbase = j * BK + g * HC;
+      int lim = min(HC, p.sk - kbase);
+      if (p.causal) lim = min(lim, causal_limit(qg, p.k_offset + kbase, HC));
+      if (!__all_sync(0xffffffffu, lim == HC)) {
+#pragma unroll
+        for (int e = 0; e < HC; e++) x[e] = (e < lim) ? x[e] : -INFINITY;
+      }
+      float mx[4];
+#pragma unroll
+      for (int t = 0; t < 4; t++) mx[t] = -INFINITY;
+#pragma unroll
+      for (int e = 0; e < HC; e += 8) {
+        const int t = (e >> 3) & 3;
+        mx[t] = fmax3(mx[t], x[e], x[e + 1]);
+        mx[t] = fmax3(mx[t], x[e + 2], x[e + 3]);
+        mx[t] = fmax3(mx[t], x[e + 4], x[e + 5]);
+        mx[t] = fmax3(mx[t], x[e + 6], x[e + 7]);
+      }
+      const float mx_half = fmax3(mx[0], mx[1], fmaxf(mx[2], mx[3]));
+      float* slot = red + (j & 1) * 256;
+      slot[g * 128 + r] = mx_half;
+      if (bar_any(1, 256, !w)) {  // uniform across both warpgroups
+        ok = false;
+        break;
+      }
+#ifdef FA_TRACE
+      if (threadIdx.x == 128 && leader) atomicAdd(&g_fa_trace[12], (unsigned long long)(clock64() - tr_a));
+      tr_a = clock64();
+#endif
+      const float mx_row = fmaxf(mx_half, slot[(g ^ 1) * 128 + r]);
+      // Both halves hold the same m and see the same mx_row, so they take
+      // identical rescale decisions.
+      const float m_new = fmaxf(m, mx_row * c_log2);
+      float corr = 1.0f;
+      bool need = false;
+      if (m == -INFINITY) {
+        m = m_new;
+      } else if (m_new > m + kRescaleLog2) {
+        need = true;
+        corr = ex2(m - m_new);
+        m = m_new;
+      }
+      if (__any_sync(0xffffffffu, need) &&
+          __all_sync(0xffffffffu, mbar_wait(bar_o_done, (j - 1) & 1, abort_flag, p.err))) {
+        // (a failed wait raises the abort flag; the loop then ends at the
+        // next tile's bar_any)
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < HD / 32; c++) {
+          uint32_t rr[32];
+          tmem_ld32(t_o + lane_off + g * HD + c * 32, rr);
+          tmem_wait_ld_regs(rr);
+#pragma unroll
+          for (int e = 0; e < 32; e++) rr[e] = __float_as_uint(__uint_as_float(rr[e]) * corr);
+          tmem_st32(t_o + lane_off + g * HD + c * 32, rr);
+        }
+        l *= corr;
+      }
+      const float neg_m = (m == -INFINITY) ? 0.0f : -m;
+      float rs[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int c = 0; c < HC / 32; c++) {
+        uint32_t rr[32];
+#pragma unroll
+        for (int e = 0; e < 32; e++) {
+          const uint32_t t = __float_as_uint(ex2(fmaf(x[c * 32 + e], c_log2, neg_m))) & 0xFFFFE000u;
+          rs[e & 3] += __uint_as_float(t);
+          rr[e] = t;
+        }
+        tmem_st32(t_s(b) + lane_off + g * HC + c * 32, rr);
+      }
+      l += (rs[0] + rs[1]) + (rs[2] + rs[3]);
+#ifdef FA_TRACE
+      if (threadIdx.x == 128 && leader) atomicAdd(&g_fa_trace[13], (unsigned long long)(clock64() - tr_a));
+      tr_a = clock64();
+#endif
+      tmem_wait_st();
+#ifdef FA_TRACE
+      if (threadIdx.x == 128 && leader) atomicAdd(&g_fa_trace[14], (unsigned long long)(clock64() - tr_a));
+      tr_a = clock64();
+#endif
+      tc_fence_before();
+      warp_arrive_leader(bar_p_full(b));
+#ifdef FA_TRACE
+      if (threadIdx.x == 128 && leader) atomicAdd(&g_fa_trace[15], (unsigned long long)(clock64() - tr_a));
+#endif
+      if (threadIdx.x == 128) FA_EV(5, j);
+      if (threadIdx.x == 256) FA_EV(7, j);
+      if (threadIdx.x == 128 && leader) {
+        FA_TR_ADD(6);
+        FA_TR_CNT(8);
+      }
+    }
+    if (n_kv > 0 && ok) ok = __all_sync(0xffffffffu, mbar_wait(bar_o_final, 0, abort_flag, p.err));
+    if (*abort_flag) ok = false;
+    // full row sum = both halves' partial sums (all 8 softmax warps reach this
+    // barrier on every path: the loop above is left only uniformly)
+    red[512 + g * 128 + r] = l;
+    ok = !bar_any(1, 256, !ok);
+    const float l_row = l + red[512 + (g ^ 1) * 128 + r];
+    if (ok) {
+      tc_fence_after();
+      const float inv_l = l_row > 0.0f ? 1.0f / l_row : 0.0f;
+      const bool row_ok = r < q_rows;
+      float* orow = p.o + ((size_t)bh * p.sq + q0 + r) * D + g * HD;
+#pragma unroll
+      for (int c = 0; c < HD / 32; c++) {
+        uint32_t rr[32];
+        if (n_kv > 0) {
+          tmem_ld32(t_o + lane_off + g * HD + c * 32, rr);
+          tmem_wait_ld_regs(rr);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; e++) rr[e] = 0u;
+        }
+        if (row_ok) {
+#pragma unroll
+          for (int e = 0; e < 32; e += 4) {
+            float4 v4 = make_float4(__uint_as_float(rr[e]) * inv_l, __uint_as_float(rr[e + 1]) * inv_l,
+                                    __uint_as_float(rr[e + 2]) * inv_l,
+                                    __uint_as_float(rr[e + 3]) * inv_l);
+            *reinterpret_cast<float4*>(orow + c * 32 + e) = v4;
+          }
+        }
+      }
+      if (row_ok && g == 0 && p.lse)
+        p.lse[(size_t)bh * p.sq + q0 + r] =
+            l_row > 0.0f ? (m + __log2f(l_row)) * 0.69314718055994530942f : -INFINITY;
+    }
+  }
+  // Every MMA of the pair (which reads both CTAs' shared memory and writes both
+  // CTAs' TMEM) completes before either CTA frees TMEM or exits.
+  if (warp == 1 && lane == 0 && !skip) {
+    volatile int no_abort = 0;
+    mbar_wait(bar_drain, 0, &no_abort, p.err);
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();
+#ifdef FA_TRACE
+  if (threadIdx.x == 0 && leader) {
+    atomicAdd(&g_fa_trace[9], (unsigned long long)(clock64() - tr_kstart));
+    atomicAdd(&g_fa_trace[10], 1ull);
+  }
+#endif
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem),
                  "r"((uint32_t)C::kTmemCols)
                  : "memory");
   }
@@ -609,7 +1250,63 @@ cudaError_t launch_tf32(const FwdParams& p, cudaStream_t s) {
   return cudaGetLastError();
 }
 
+template <int D, int BK, int NKS, int NVS>
+cudaError_t launch_tf32_pair(const FwdParams& p, cudaStream_t s) {
+  using C = PairCfg<D, BK, NKS, NVS>;
+  CUtensorMap mk, mv;
+  if (!make_map(&mk, p.k, D, p.sk, p.bh, BK / 2, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !make_map(&mv, p.v, D, p.sk, p.bh, BK, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B))
+    return cudaErrorInvalidValue;
+  static std::atomic<unsigned long long> attr_set{0};  // one bit per device
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (!(attr_set.load() & bit)) {
+    cudaError_t e = cudaFuncSetAttribute(tc_fwd_tf32_pair<D, BK, NKS, NVS>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         C::kSmemBytes);
+    if (e != cudaSuccess) return e;
+    attr_set.fetch_or(bit);
+  }
+  const int n_pairs = (p.sq + 2 * kBM - 1) / (2 * kBM);
+  // grid.y holds the slice index (at most 65535 per launch)
+  for (int b0 = 0; b0 < p.bh; b0 += 65535) {
+    FwdParams q = p;
+    q.bh = min(65535, p.bh - b0);
+    CUtensorMap qk = mk, qv = mv;
+    if (b0 > 0) {
+      q.q += (size_t)b0 * p.sq * D;
+      q.o += (size_t)b0 * p.sq * D;
+      if (q.lse) q.lse += (size_t)b0 * p.sq;
+      q.k += (size_t)b0 * p.sk * D;
+      q.v += (size_t)b0 * p.sk * D;
+      if (!make_map(&qk, q.k, D, p.sk, q.bh, BK / 2, CU_TENSOR_MAP_SWIZZLE_128B) ||
+          !make_map(&qv, q.v, D, p.sk, q.bh, BK, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B))
+        return cudaErrorInvalidValue;
+    }
+    dim3 grid(2, q.bh, n_pairs);
+    tc_fwd_tf32_pair<D, BK, NKS, NVS><<<grid, kThreadsPair, C::kSmemBytes, s>>>(qk, qv, q);
+    count_launch();
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
 }  // namespace
+
+#ifdef FA_TRACE
+extern "C" __attribute__((visibility("default"))) int fa_events_read(long long* out) {
+  cudaDeviceSynchronize();
+  return (int)cudaMemcpyFromSymbol(out, g_fa_events, sizeof(g_fa_events));
+}
+extern "C" __attribute__((visibility("default"))) int fa_trace_read(unsigned long long* out) {
+  cudaDeviceSynchronize();
+  cudaMemcpyFromSymbol(out, g_fa_trace, sizeof(g_fa_trace));
+  unsigned long long z[32] = {0};
+  return (int)cudaMemcpyToSymbol(g_fa_trace, z, sizeof(z));
+}
+#endif
 
 bool tc_supported(int d, int precision) {
   return precision == 0 && (d == 64 || d == 128);
@@ -620,7 +1317,15 @@ size_t tc_scratch_floats(const FwdParams&, int) { return 0; }
 cudaError_t launch_tc(const FwdParams& p, int precision, float*, size_t, cudaStream_t s) {
   if (precision != 0) return cudaErrorInvalidValue;
   if (p.sq > 65535 * kBM) return cudaErrorInvalidValue;
-  if (p.d == 128) return launch_tf32<128, 128, 64, 2, 3>(p, s);
+#ifndef FA_D128_VK
+#define FA_D128_VK 64
+#define FA_D128_NVS 3
+#endif
+#ifdef FA_D128_SINGLE_CTA
+  if (p.d == 128) return launch_tf32<128, 128, FA_D128_VK, 2, FA_D128_NVS>(p, s);
+#else
+  if (p.d == 128) return launch_tf32_pair<128, 128, 3, 3>(p, s);
+#endif
   if (p.d == 64) return launch_tf32<64, 128, 128, 3, 3>(p, s);
   return cudaErrorInvalidValue;
 }
