@@ -159,6 +159,27 @@ __device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_
       : "memory");
 }
 
+// Warp-wide forms: every lane executes them with uniform operands (so the
+// compiler keeps descriptors in uniform registers) and one elected lane issues.
+__device__ __forceinline__ void mma_ts_elect(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                             uint32_t idesc, uint32_t accum) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accum)
+      : "memory");
+}
+__device__ __forceinline__ void tc_commit_elect(uint32_t bar) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(
+          bar)
+      : "memory");
+}
+
 #define FA_R8(b) "=r"(r[b + 0]), "=r"(r[b + 1]), "=r"(r[b + 2]), "=r"(r[b + 3]), \
                  "=r"(r[b + 4]), "=r"(r[b + 5]), "=r"(r[b + 6]), "=r"(r[b + 7])
 #define FA_W8(b) "r"(r[b + 0]), "r"(r[b + 1]), "r"(r[b + 2]), "r"(r[b + 3]), \
@@ -391,65 +412,64 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncwarp();
   } else if (warp == 1) {
-    // ------------------------------ MMA issuer
-    if (lane == 0 && !skip) {
+    // ------------------------------ MMA issuer (whole warp; one elected lane issues)
+    if (!skip) {
       constexpr uint32_t idesc_qk = instr_desc(kBM, BK, false);
       constexpr uint32_t idesc_pv = instr_desc(kBM, D, true);
-      bool ok = mbar_wait(bar_q_full, 0, abort_flag, p.err);
+      bool ok = __all_sync(0xffffffffu, mbar_wait(bar_q_full, 0, abort_flag, p.err));
       tc_fence_after();
       auto issue_pv = [&](int jj) -> bool {
         const int b = jj & 1;
         {
           FA_TR_T0();
-          if (!mbar_wait(bar_p_full(b), (jj >> 1) & 1, abort_flag, p.err)) return false;
-          FA_TR_ADD(3);
+          if (!__all_sync(0xffffffffu, mbar_wait(bar_p_full(b), (jj >> 1) & 1, abort_flag, p.err)))
+            return false;
+          if (lane == 0) FA_TR_ADD(3);
         }
 #pragma unroll
         for (int h = 0; h < VS; h++) {
           const int g = jj * VS + h, sv = g % NVS;
           {
             FA_TR_T0();
-            if (!mbar_wait(bar_v_full(sv), (g / NVS) & 1, abort_flag, p.err)) return false;
-            FA_TR_ADD(4);
+            if (!__all_sync(0xffffffffu, mbar_wait(bar_v_full(sv), (g / NVS) & 1, abort_flag, p.err)))
+              return false;
+            if (lane == 0) FA_TR_ADD(4);
           }
           tc_fence_after();
-          const uint32_t vbase = sV + sv * C::kVBytes;
+          // 8 keys = two 4-row groups (SBO = 512 B); 32-column chunks LBO apart
+          const uint64_t vdesc =
+              smem_desc(sV + sv * C::kVBytes, VK * 128, 512, kLayoutSw128Base32);
 #pragma unroll
-          for (int kk = 0; kk < VK / 8; kk++) {
-            // 8 keys = two 4-row groups (SBO = 512 B); 32-column chunks LBO apart
-            const uint64_t bdesc =
-                smem_desc(vbase + kk * 1024, VK * 128, 512, kLayoutSw128Base32);
-            mma_ts(t_o, t_s(b) + h * VK + kk * 8, bdesc, idesc_pv,
-                   (jj > 0 || h > 0 || kk > 0) ? 1u : 0u);
-          }
-          tc_commit(bar_v_empty(sv));
+          for (int kk = 0; kk < VK / 8; kk++)
+            mma_ts_elect(t_o, t_s(b) + h * VK + kk * 8, vdesc + (uint64_t)(kk * 64), idesc_pv,
+                         (jj > 0 || h > 0 || kk > 0) ? 1u : 0u);
+          tc_commit_elect(bar_v_empty(sv));
         }
-        tc_commit(bar_o_done);
+        tc_commit_elect(bar_o_done);
         return true;
       };
       for (int j = 0; j < n_kv && ok; j++) {
         const int s = j % NKS, b = j & 1;
         {
           FA_TR_T0();
-          ok = mbar_wait(bar_k_full(s), (j / NKS) & 1, abort_flag, p.err);
-          FA_TR_ADD(2);
+          ok = __all_sync(0xffffffffu, mbar_wait(bar_k_full(s), (j / NKS) & 1, abort_flag, p.err));
+          if (lane == 0) FA_TR_ADD(2);
         }
         if (!ok) break;
         tc_fence_after();
-        const uint32_t kbase = sK + s * C::kKBytes;
+        const uint64_t kdesc = smem_desc(sK + s * C::kKBytes, 16, 1024, kLayoutSw128);
 #pragma unroll
-        for (int kk = 0; kk < D / 8; kk++) {
-          const uint64_t bdesc =
-              smem_desc(kbase + (kk >> 2) * BK * 128 + (kk & 3) * 32, 16, 1024, kLayoutSw128);
-          mma_ts(t_s(b), t_q + kk * 8, bdesc, idesc_qk, kk > 0 ? 1u : 0u);
-        }
-        tc_commit(bar_s_full(b));
-        tc_commit(bar_k_empty(s));
+        for (int kk = 0; kk < D / 8; kk++)
+          mma_ts_elect(t_s(b), t_q + kk * 8,
+                       kdesc + (uint64_t)(((kk >> 2) * BK * 128 + (kk & 3) * 32) >> 4), idesc_qk,
+                       kk > 0 ? 1u : 0u);
+        tc_commit_elect(bar_s_full(b));
+        tc_commit_elect(bar_k_empty(s));
         if (j > 0) ok = issue_pv(j - 1);
       }
-      if (ok && n_kv > 0 && issue_pv(n_kv - 1)) tc_commit(bar_o_final);
-      // Drain: all MMAs issued by this thread complete before TMEM is freed.
-      tc_commit(bar_drain);
+      if (ok && n_kv > 0 && issue_pv(n_kv - 1)) tc_commit_elect(bar_o_final);
+      // Drain: all MMAs issued by this warp complete before TMEM is freed.
+      tc_commit_elect(bar_drain);
       volatile int no_abort = 0;
       mbar_wait(bar_drain, 0, &no_abort, p.err);
     }
@@ -1321,12 +1341,13 @@ cudaError_t launch_tc(const FwdParams& p, int precision, float*, size_t, cudaStr
 #define FA_D128_VK 64
 #define FA_D128_NVS 3
 #endif
-#ifdef FA_D128_SINGLE_CTA
-  if (p.d == 128) return launch_tf32<128, 128, FA_D128_VK, 2, FA_D128_NVS>(p, s);
-#else
-  if (p.d == 128) return launch_tf32_pair<128, 128, 3, 3>(p, s);
-#endif
-  if (p.d == 64) return launch_tf32<64, 128, 128, 3, 3>(p, s);
+  // A pair covers 256 query rows; a single 128-row tile runs on one SM.
+  const bool single = p.sq <= kBM;
+  if (p.d == 128)
+    return single ? launch_tf32<128, 128, FA_D128_VK, 2, FA_D128_NVS>(p, s)
+                  : launch_tf32_pair<128, 128, 3, 3>(p, s);
+  if (p.d == 64)
+    return single ? launch_tf32<64, 128, 128, 3, 3>(p, s) : launch_tf32_pair<64, 128, 3, 3>(p, s);
   return cudaErrorInvalidValue;
 }
 
