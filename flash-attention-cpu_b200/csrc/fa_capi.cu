@@ -374,6 +374,51 @@ int fa_lse_combine_device(const float* o_parts, const float* lse_parts, size_t n
   return FA_OK;
 }
 
+int fa_forward_decode_noalloc(const float* q, const float* k, const float* v, float* out,
+                              float* lse, size_t bh, size_t sq, size_t sk, size_t d, int causal,
+                              void* stream) {
+  t_err.clear();
+  if (bh == 0 || sq == 0 || sk == 0 || d == 0) return FA_OK;
+  if (!q || !k || !v || !out) return set_err(FA_ERR_ARG, "null buffer pointer");
+  if (sq > 16 || !fa::decode_supported((int)d))
+    return set_err(FA_ERR_UNSUPPORTED,
+                   "fa_forward_decode_noalloc handles seq_len_q <= 16 and d_head % 4 == 0, "
+                   "d_head <= 256");
+  if (bh > 65535 || sk > (size_t)INT32_MAX)
+    return set_err(FA_ERR_UNSUPPORTED, "fa_forward_decode_noalloc: batch_heads > 65535");
+  // Device checks without the library's lazy set-up (which allocates).
+  int dev = 0, major = 0, sms = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return set_err(FA_ERR_NO_DEVICE, std::string("no usable CUDA device: ") + cudaGetErrorString(e));
+  }
+  if (major != 10) return set_err(FA_ERR_NO_DEVICE, "this library is built for sm_100a (B200) only");
+  const int splits = fa::decode_pick_splits((int)bh, (int)sq, (int)sk, sms);
+  const size_t need = splits > 1 ? (size_t)splits * bh * sq * (d + 1) : 0;
+  if (need > fa::static_scratch_floats())
+    return set_err(FA_ERR_UNSUPPORTED,
+                   "fa_forward_decode_noalloc: needs " + std::to_string(need) +
+                       " floats of scratch, the fixed limit is " +
+                       std::to_string(fa::static_scratch_floats()));
+  float* scratch = nullptr;
+  e = fa::static_scratch_ptr(&scratch);
+  if (e != cudaSuccess) return cuda_err(e, "cudaGetSymbolAddress(decode scratch)");
+  fa::FwdParams p{};
+  p.q = q; p.k = k; p.v = v; p.o = out; p.lse = lse;
+  p.bh = (int)bh; p.sq = (int)sq; p.sk = (int)sk; p.d = (int)d;
+  p.causal = causal ? 1 : 0;
+  p.scale = 1.0f / sqrtf((float)p.d);
+  p.scale_log2 = p.scale * 1.4426950408889634f;
+  p.err = nullptr;  // the decode kernels have no bounded waits
+  e = fa::launch_decode(p, splits, scratch, (cudaStream_t)stream);
+  if (e != cudaSuccess) return cuda_err(e, "decode launch");
+  t_path = "decode_splitkv_noalloc";
+  return FA_OK;
+}
+
 int fa_sync_status(void* stream) {
   t_err.clear();
   int dev = 0;

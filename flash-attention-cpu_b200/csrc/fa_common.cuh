@@ -69,6 +69,9 @@ cudaError_t launch_combine(const float* o_parts, const float* lse_parts, int n_p
                            long long rows, int d, float* out, float* lse_out,
                            cudaStream_t s);
 bool decode_supported(int d);
+// Fixed device array used by the allocation-free decode entry point.
+size_t static_scratch_floats();
+cudaError_t static_scratch_ptr(float** out);
 // tcgen05 family.  tc_supported() says whether a tensor-core kernel exists for d.
 bool tc_supported(int d, int precision);
 cudaError_t launch_tc(const FwdParams& p, int precision, float* scratch,

@@ -12,6 +12,8 @@
 
 #include <math.h>
 
+#include <mutex>
+
 namespace fa {
 
 namespace {
@@ -363,6 +365,43 @@ cudaError_t launch_combine(const float* o_parts, const float* lse_parts, int n_p
                                              lse_out);
   count_launch();
   return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// Fixed scratch for the allocation-free decode entry point.  Some callers of
+// this library cannot allocate device memory at call time (for example code
+// running under an allocator that forbids new device allocations, or an
+// embedding runtime that owns all device memory and hands out only its own
+// buffers).  For them the split partials of the decode kernel live in this
+// file-scope array instead of a per-call allocation.  Every GPU that loads
+// the library holds it (4 MiB) until the process exits.  All calls on a
+// device share it, so calls whose kernels overlap on that GPU race; each call
+// overwrites every partial it later reads, so nothing needs clearing.
+constexpr size_t kStaticScratchFloats = size_t(1) << 20;
+static __device__ __align__(256) float g_decode_scratch[kStaticScratchFloats];
+
+size_t static_scratch_floats() { return kStaticScratchFloats; }
+
+// Device address of the array on the current device.  In host code the
+// array's name is only a host-side stand-in, so the address is looked up once
+// per device with that device current, and cached.
+cudaError_t static_scratch_ptr(float** out) {
+  constexpr int kMaxDev = 64;
+  static std::mutex mu;
+  static float* cache[kMaxDev] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxDev) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!cache[dev]) {
+    float* ptr = nullptr;
+    e = cudaGetSymbolAddress((void**)&ptr, g_decode_scratch);
+    if (e != cudaSuccess) return e;
+    cache[dev] = ptr;
+  }
+  *out = cache[dev];
+  return cudaSuccess;
 }
 
 }  // namespace fa

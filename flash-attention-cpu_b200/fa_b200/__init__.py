@@ -34,7 +34,7 @@ __all__ = [
     "flash_attention_v1", "flash_attention_v2", "flash_attention_v3", "flash_attention",
     "flash_attention_multihead_v1", "flash_attention_multihead_v2",
     "flash_attention_multihead_v3", "flash_attention_multihead",
-    "multihead_lse", "forward_device", "forward_partial_device", "lse_combine_device",
+    "multihead_lse", "forward_device", "forward_decode_noalloc", "forward_partial_device", "lse_combine_device",
     "set_precision", "get_precision", "launch_count", "last_path", "sync_status",
     "device_count", "lib_path", "PREC_TF32", "PREC_3XTF32", "PREC_FP32",
 ]
@@ -108,6 +108,8 @@ def _load():
     L.fa_forward_partial_device.argtypes = [_P, _P, _P, _P, _P, _SZ, _SZ, _SZ, _SZ, ctypes.c_int,
                                             _SZ, _SZ, _P]
     L.fa_forward_partial_device.restype = ctypes.c_int
+    L.fa_forward_decode_noalloc.argtypes = [_P, _P, _P, _P, _P, _SZ, _SZ, _SZ, _SZ, ctypes.c_int, _P]
+    L.fa_forward_decode_noalloc.restype = ctypes.c_int
     L.fa_lse_combine_device.argtypes = [_P, _P, _SZ, _SZ, _SZ, _P, _P, _P]
     L.fa_lse_combine_device.restype = ctypes.c_int
     L.fa_sync_status.argtypes = [_P]
@@ -251,6 +253,21 @@ def forward_partial_device(q, k, v, out, lse, causal, q_offset, k_offset, stream
     _check(_load().fa_forward_partial_device(
         _dptr(q, "q"), _dptr(k, "k"), _dptr(v, "v"), _dptr(out, "out"), _dptr(lse, "lse"),
         bh, sq, sk, d, int(bool(causal)), int(q_offset), int(k_offset), _stream(stream)))
+
+
+def forward_decode_noalloc(q, k, v, out, lse=None, causal=False, stream=None):
+    """Decode forward (seq_len_q <= 16) that allocates no device memory: the
+    split partials use the library's fixed device array.  For callers that may
+    not allocate while running; calls that overlap on one GPU race."""
+    bh, sq, d = q.shape
+    sk = k.shape[1]
+    if tuple(k.shape) != (bh, sk, d) or tuple(v.shape) != (bh, sk, d) or \
+            tuple(out.shape) != (bh, sq, d):
+        raise Panic("device shape mismatch")
+    _check(_load().fa_forward_decode_noalloc(
+        _dptr(q, "q"), _dptr(k, "k"), _dptr(v, "v"), _dptr(out, "out"),
+        _dptr(lse, "lse") if lse is not None else None, bh, sq, sk, d, int(bool(causal)),
+        _stream(stream)))
 
 
 def lse_combine_device(o_parts, lse_parts, out, lse_out=None, stream=None):

@@ -159,6 +159,24 @@ FA_API int fa_lse_combine_device(const float* o_parts, const float* lse_parts, s
                           size_t rows, size_t d_head, float* out, float* lse_out,
                           void* stream);
 
+/* Allocation-free variant of the decode (few query rows) forward, for callers
+ * that cannot allocate device memory while they run: code under an allocator
+ * that forbids new device allocations, or a runtime that owns all device
+ * memory and hands out only its own buffers.  No counterpart in the reference
+ * (the crate never allocates device memory).  Same inputs, outputs and results
+ * as fa_forward_device for seq_len_q <= 16, d_head % 4 == 0, d_head <= 256,
+ * batch_heads <= 65535; the split partials live in a fixed 4 MiB device array
+ * of this library (held on every GPU that loads it until exit) instead of a
+ * per-call allocation, and a shape needing more than that is rejected with
+ * FA_ERR_UNSUPPORTED.  The first call on a device looks the array's address
+ * up (a CUDA runtime query, no allocation); make that first call before any
+ * stream capture.  All calls on a device share the array: calls whose kernels
+ * overlap on the GPU race (serialise them on one stream).  Device buffers,
+ * asynchronous on `stream`. */
+FA_API int fa_forward_decode_noalloc(const float* q, const float* k, const float* v, float* out,
+                                     float* lse, size_t batch_heads, size_t seq_len_q,
+                                     size_t seq_len_k, size_t d_head, int causal, void* stream);
+
 /* Waits for `stream` and reports whether any kernel this library enqueued on
  * the current device has hit its bounded-wait limit since the last check
  * (FA_ERR_TIMEOUT; the flag is then cleared).  The device-resident calls are
