@@ -242,9 +242,12 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ref-budget", type=float, default=8.0)
+    ap.add_argument("--bh", type=int, default=0,
+                    help="override the slice count (smaller cases for profiler captures)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    args.e2e_steps = max(1, args.e2e_steps)
     if args.impl == "reference":
         return run_reference(args)
 
@@ -257,6 +260,8 @@ def main():
     fa_b200.set_device(torch.cuda.current_device())
     fa_b200.set_precision(PRECISION_NAMES[args.precision])
     cfg = CONFIGS[args.config]
+    if args.bh > 0:
+        cfg = (args.bh,) + cfg[1:]
     bh, sq, sk, d, causal, seed, factor, _ = cfg
     dev = torch.device("cuda", torch.cuda.current_device())
 
