@@ -221,6 +221,100 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def run_kv_split(args, cfg, rank, world, local, dev):
+    """Config 5 across `world` GPUs: one 131072-long causal slice whose keys are
+    split zig-zag over the ranks, partials merged after one all-to-all (NCCL).
+    The total work is fixed, so this is strong scaling."""
+    import torch
+    import torch.distributed as dist
+    import fa_b200
+    from fa_b200.kvsplit import kv_split_forward, zigzag_chunks
+    if world == 1 and not dist.is_initialized():
+        dist.init_process_group("nccl", init_method="tcp://127.0.0.1:29533", rank=0,
+                                world_size=1, device_id=dev)
+    bh, sq, sk, d, causal, seed, factor, _ = cfg
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(seed)
+    q = torch.randn(1, sq, d, device=dev, generator=gen) * factor
+    k_meta = torch.empty(1, sk, d, device="meta")
+    chunks = zigzag_chunks(sk, world, rank)
+    kc = [torch.randn(1, c.stop - c.start, d, device=dev, generator=gen) * factor for c in chunks]
+    vc = [torch.randn(1, c.stop - c.start, d, device=dev, generator=gen) * factor for c in chunks]
+
+    def step():
+        return kv_split_forward(q, k_meta, k_meta, causal, k_chunks=kc, v_chunks=vc)
+
+    stream = torch.cuda.current_stream()
+    clk = ClockSampler(local).__enter__()
+    time.sleep(0.3)
+    for _ in range(args.warmup):
+        step()
+    fa_b200.sync_status(stream)
+    dist.barrier()
+    torch.cuda.synchronize()
+    launches0 = fa_b200.launch_count()
+    wall0 = time.time()
+    t0e, t1e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0e.record(stream)
+    for _ in range(args.steps):
+        out, lse, _rows = step()
+    t1e.record(stream)
+    torch.cuda.synchronize()
+    wall1 = time.time()
+    time.sleep(0.25)
+    clk.__exit__(None, None, None)
+    launches = fa_b200.launch_count() - launches0
+    t = torch.tensor([t0e.elapsed_time(t1e) / args.steps], device=dev, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    step_ms = float(t.item())
+    fl = flops_of(1, sq, sk, d, causal)
+    value = fl / (step_ms * 1e-3) / 1e12
+    # end to end: Q and this rank's K/V chunks from pinned host memory, the
+    # owned output rows back to pinned host memory, every step
+    hq = torch.empty_like(q, device="cpu").pin_memory()
+    hq.copy_(q)
+    hk = [x.cpu().pin_memory() for x in kc]
+    hv = [x.cpu().pin_memory() for x in vc]
+    ho = torch.empty(sq // world, d).pin_memory()
+    dist.barrier()
+    te0 = time.perf_counter()
+    for _ in range(args.e2e_steps):
+        q.copy_(hq, non_blocking=True)
+        for a, b in zip(kc, hk):
+            a.copy_(b, non_blocking=True)
+        for a, b in zip(vc, hv):
+            a.copy_(b, non_blocking=True)
+        out, lse, _rows = step()
+        ho.copy_(out, non_blocking=True)
+        torch.cuda.synchronize()
+    te = torch.tensor([(time.perf_counter() - te0) / args.e2e_steps], device=dev,
+                      dtype=torch.float64)
+    dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_s = float(te.item())
+    kv_bytes = sum(4 * 2 * (c.stop - c.start) * d for c in chunks)
+    if rank == 0:
+        peaks = measured_peaks()
+        peak = (peaks["bf16_tflops"] / 2 if peaks else 795.0) * world
+        line = {"metric": "attention TFLOP/s", "value": value, "unit": "TFLOP/s",
+                "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": step_ms, "higher_is_better": True, "scaling": "strong",
+                "vs_baseline": None, "dtype": "tf32", "data": "synthetic",
+                "config": dict(config_dict(args, cfg, world),
+                               parallelism=f"kv-split over {world} GPUs (zig-zag chunks, "
+                                           "one all-to-all of partials, LSE merge)"),
+                "clocks": clk.summary(wall0, wall1),
+                "e2e": {"value": fl / e2e_s / 1e12, "unit": "TFLOP/s",
+                        "h2d_bytes_per_step": 4 * sq * d + kv_bytes,
+                        "d2h_bytes_per_step": 4 * (sq // world) * d, "ms_per_step": e2e_s * 1e3,
+                        "api": "fa_b200.kvsplit.kv_split_forward"},
+                "gpu_launches": launches,
+                "roofline": {"bound": "tensor", "achieved": value, "peak": peak,
+                             "unit": "TFLOP/s", "frac": value / peak, "traffic": None,
+                             "peak_source": f"{world} x dense TF32 = measured bf16 burst / 2"}}
+        print(json.dumps(line), flush=True)
+    dist.destroy_process_group()
+
+
 def config_dict(args, cfg, world):
     bh, sq, sk, d, causal, seed, factor, desc = cfg
     return {"workload": f"{args.config}: {desc}", "batch_heads_per_gpu": bh, "seq_len_q": sq,
@@ -242,6 +336,8 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ref-budget", type=float, default=8.0)
+    ap.add_argument("--kv-split", action="store_true",
+                    help="config 5 through the key-range split even on one GPU")
     ap.add_argument("--bh", type=int, default=0,
                     help="override the slice count (smaller cases for profiler captures)")
     args = ap.parse_args()
@@ -264,6 +360,8 @@ def main():
         cfg = (args.bh,) + cfg[1:]
     bh, sq, sk, d, causal, seed, factor, _ = cfg
     dev = torch.device("cuda", torch.cuda.current_device())
+    if args.config == "c5" and (world > 1 or args.kv_split):
+        return run_kv_split(args, cfg, rank, world, local, dev)
 
     # inputs of this rank's slices: the config's generator, offset per rank
     gen = torch.Generator(device=dev)

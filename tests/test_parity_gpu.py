@@ -258,3 +258,27 @@ def test_partial_ranges_and_lse_combine(fa, prec):
     tol = TOL[prec]
     assert max_abs_diff(out.cpu().numpy().ravel(), want) < tol
     assert max_abs_diff(lse.cpu().numpy().ravel(), wlse) < tol
+
+
+def test_kv_split_one_rank_nccl(fa):
+    # The multi-GPU key-range split through the real kernels and NCCL with one
+    # rank (zig-zag chunks, partial kernels, all-to-all, LSE merge).
+    import torch
+    import torch.distributed as dist
+    from fa_b200.kvsplit import kv_split_forward
+    fa.set_precision(fa.PREC_TF32)
+    rows, d = 1000, 128
+    q, k, v = (random_vec(rows * d, s) for s in (41, 42, 43))
+    want, wlse = O.flash_v2(q, k, v, rows, rows, d, True)
+    dev = torch.device("cuda", 0)
+    dist.init_process_group("nccl", init_method="tcp://127.0.0.1:29541", rank=0, world_size=1,
+                            device_id=dev)
+    try:
+        t = [torch.from_numpy(x).to(dev).view(1, rows, d) for x in (q, k, v)]
+        out, lse, (a, b) = kv_split_forward(t[0], t[1], t[2], True)
+        torch.cuda.synchronize()
+    finally:
+        dist.destroy_process_group()
+    assert (a, b) == (0, rows)
+    assert max_abs_diff(out.cpu().numpy().ravel(), want) < 2e-3
+    assert max_abs_diff(lse.cpu().numpy(), wlse) < 2e-3
