@@ -145,6 +145,16 @@ int dispatch(fa::FwdParams p, int dev, cudaStream_t s) {
     if (e != cudaSuccess) return cuda_err(e, "decode launch");
     return FA_OK;
   }
+  if (prec == FA_PREC_3XTF32 && (p.d == 64 || p.d == 128)) {
+    t_path = "tcgen05_3xtf32";
+    float* ws = nullptr;
+    e = cudaMallocAsync((void**)&ws, fa::tc3_workspace_floats(p) * sizeof(float), s);
+    if (e != cudaSuccess) return cuda_err(e, "cudaMallocAsync(3xTF32 split planes)");
+    e = fa::launch_tc3(p, ws, s);
+    cudaFreeAsync(ws, s);
+    if (e != cudaSuccess) return cuda_err(e, "tcgen05 3xTF32 launch");
+    return FA_OK;
+  }
   if (fa::tc_supported(p.d, prec)) {
     t_path = prec == FA_PREC_TF32 ? "tcgen05_tf32" : "tcgen05_3xtf32";
     e = fa::launch_tc(p, prec, nullptr, 0, s);

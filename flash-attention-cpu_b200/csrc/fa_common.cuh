@@ -77,6 +77,10 @@ bool tc_supported(int d, int precision);
 cudaError_t launch_tc(const FwdParams& p, int precision, float* scratch,
                       size_t scratch_floats, cudaStream_t s);
 size_t tc_scratch_floats(const FwdParams& p, int precision);
+// 3xTF32 family (d = 64, 128): workspace of tc3_workspace_floats() floats
+// (hi/lo planes of K and V).
+size_t tc3_workspace_floats(const FwdParams& p);
+cudaError_t launch_tc3(const FwdParams& p, float* ws, cudaStream_t s);
 unsigned long long launches_issued();
 void count_launch(int n = 1);
 }  // namespace fa
