@@ -193,17 +193,21 @@ int check_err_flag(int dev, cudaStream_t s) {
   return FA_OK;
 }
 
-struct HostCallStream {
-  cudaStream_t s[kMaxDevices] = {};
-  ~HostCallStream() {}
+// Three streams per (thread, device) for the host-slice calls: host-to-device
+// copies, compute, device-to-host copies.  Large calls are cut into chunks of
+// (batch, head) slices so that the copies of one chunk overlap the compute and
+// the copies of the others (the two copy directions use separate engines).
+struct HostCallStreams {
+  cudaStream_t s[kMaxDevices][3] = {};
 };
-thread_local HostCallStream t_streams;
+thread_local HostCallStreams t_streams;
 
-int host_stream(int dev, cudaStream_t* out) {
-  if (!t_streams.s[dev]) {
-    cudaError_t e = cudaStreamCreateWithFlags(&t_streams.s[dev], cudaStreamNonBlocking);
-    if (e != cudaSuccess) return cuda_err(e, "cudaStreamCreate");
-  }
+int host_streams(int dev, cudaStream_t** out) {
+  for (int i = 0; i < 3; i++)
+    if (!t_streams.s[dev][i]) {
+      cudaError_t e = cudaStreamCreateWithFlags(&t_streams.s[dev][i], cudaStreamNonBlocking);
+      if (e != cudaSuccess) return cuda_err(e, "cudaStreamCreate");
+    }
   *out = t_streams.s[dev];
   return FA_OK;
 }
@@ -216,40 +220,64 @@ int host_forward(const float* q, const float* k, const float* v, size_t bh, size
   int dev = 0;
   int rc = prepare_device(&dev);
   if (rc) return rc;
-  cudaStream_t s;
-  if ((rc = host_stream(dev, &s))) return rc;
+  cudaStream_t* st;
+  if ((rc = host_streams(dev, &st))) return rc;
+  cudaStream_t s_in = st[0], s_comp = st[1], s_out = st[2];
   const size_t nq = bh * sq * d, nk = bh * sk * d, nl = bh * sq;
   const size_t bytes = (2 * nq + 2 * nk + nl) * sizeof(float);
+  const size_t n_chunks = (bh >= 2 && bytes >= (size_t(32) << 20)) ? (bh < 8 ? bh : 8) : 1;
+  const size_t per = (bh + n_chunks - 1) / n_chunks;
   char* buf = nullptr;
-  cudaError_t e = cudaMallocAsync((void**)&buf, bytes, s);
+  cudaError_t e = cudaMallocAsync((void**)&buf, bytes, s_in);
   if (e != cudaSuccess) return cuda_err(e, "cudaMallocAsync(staging)");
   float* dq = (float*)buf;
   float* dk = dq + nq;
   float* dv = dk + nk;
   float* dout = dv + nk;
   float* dlse = dout + nq;
-  e = cudaMemcpyAsync(dq, q, nq * sizeof(float), cudaMemcpyHostToDevice, s);
-  if (e == cudaSuccess) e = cudaMemcpyAsync(dk, k, nk * sizeof(float), cudaMemcpyHostToDevice, s);
-  if (e == cudaSuccess) e = cudaMemcpyAsync(dv, v, nk * sizeof(float), cudaMemcpyHostToDevice, s);
-  if (e != cudaSuccess) {
-    cudaFreeAsync(buf, s);
-    return cuda_err(e, "host-to-device copy");
-  }
-  fa::FwdParams p{};
-  p.q = dq; p.k = dk; p.v = dv; p.o = dout; p.lse = lse ? dlse : nullptr;
-  p.bh = (int)bh; p.sq = (int)sq; p.sk = (int)sk; p.d = (int)d;
-  p.q_offset = 0; p.k_offset = 0; p.causal = causal ? 1 : 0;
-  rc = dispatch(p, dev, s);
-  if (rc == FA_OK) rc = check_err_flag(dev, s);
-  if (rc == FA_OK) {
-    e = cudaMemcpyAsync(out, dout, nq * sizeof(float), cudaMemcpyDeviceToHost, s);
+  cudaEvent_t ev[2 * 8 + 1];
+  int n_ev = 0;
+  for (size_t i = 0; i < 2 * n_chunks + 1 && e == cudaSuccess; i++, n_ev++)
+    e = cudaEventCreateWithFlags(&ev[i], cudaEventDisableTiming);
+  for (size_t c = 0; c < n_chunks && e == cudaSuccess && rc == FA_OK; c++) {
+    const size_t h0 = c * per, h1 = (h0 + per < bh) ? h0 + per : bh;
+    if (h0 >= h1) break;
+    const size_t oq = h0 * sq * d, ok_ = h0 * sk * d, cq = (h1 - h0) * sq * d,
+                 ck = (h1 - h0) * sk * d;
+    e = cudaMemcpyAsync(dq + oq, q + oq, cq * sizeof(float), cudaMemcpyHostToDevice, s_in);
+    if (e == cudaSuccess)
+      e = cudaMemcpyAsync(dk + ok_, k + ok_, ck * sizeof(float), cudaMemcpyHostToDevice, s_in);
+    if (e == cudaSuccess)
+      e = cudaMemcpyAsync(dv + ok_, v + ok_, ck * sizeof(float), cudaMemcpyHostToDevice, s_in);
+    if (e == cudaSuccess) e = cudaEventRecord(ev[2 * c], s_in);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(s_comp, ev[2 * c], 0);
+    if (e != cudaSuccess) break;
+    fa::FwdParams p{};
+    p.q = dq + oq; p.k = dk + ok_; p.v = dv + ok_; p.o = dout + oq;
+    p.lse = lse ? dlse + h0 * sq : nullptr;
+    p.bh = (int)(h1 - h0); p.sq = (int)sq; p.sk = (int)sk; p.d = (int)d;
+    p.q_offset = 0; p.k_offset = 0; p.causal = causal ? 1 : 0;
+    rc = dispatch(p, dev, s_comp);
+    if (rc != FA_OK) break;
+    e = cudaEventRecord(ev[2 * c + 1], s_comp);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(s_out, ev[2 * c + 1], 0);
+    if (e == cudaSuccess)
+      e = cudaMemcpyAsync(out + oq, dout + oq, cq * sizeof(float), cudaMemcpyDeviceToHost, s_out);
     if (e == cudaSuccess && lse)
-      e = cudaMemcpyAsync(lse, dlse, nl * sizeof(float), cudaMemcpyDeviceToHost, s);
-    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
-    if (e != cudaSuccess) rc = cuda_err(e, "device-to-host copy");
+      e = cudaMemcpyAsync(lse + h0 * sq, dlse + h0 * sq, (h1 - h0) * sq * sizeof(float),
+                          cudaMemcpyDeviceToHost, s_out);
   }
-  cudaFreeAsync(buf, s);
-  cudaStreamSynchronize(s);
+  // everything done before the staging buffer is freed on s_in
+  cudaError_t e2 = cudaEventRecord(ev[n_ev - 1], s_out);
+  if (e2 == cudaSuccess) e2 = cudaStreamWaitEvent(s_in, ev[n_ev - 1], 0);
+  cudaError_t e3 = cudaStreamSynchronize(s_out);
+  cudaStreamSynchronize(s_comp);
+  if (e == cudaSuccess) e = e2 != cudaSuccess ? e2 : e3;
+  if (rc == FA_OK && e != cudaSuccess) rc = cuda_err(e, "host staging");
+  if (rc == FA_OK) rc = check_err_flag(dev, s_in);
+  cudaFreeAsync(buf, s_in);
+  cudaStreamSynchronize(s_in);
+  for (int i = 0; i < n_ev; i++) cudaEventDestroy(ev[i]);
   return rc;
 }
 
@@ -469,14 +497,14 @@ uint64_t fa_launch_count(void) { return fa::launches_issued(); }
 const char* fa_last_path(void) { return t_path; }
 
 void fa_shutdown(void) {
-  for (int d = 0; d < kMaxDevices; d++) {
-    if (t_streams.s[d]) {
-      cudaSetDevice(d);
-      cudaStreamSynchronize(t_streams.s[d]);
-      cudaStreamDestroy(t_streams.s[d]);
-      t_streams.s[d] = nullptr;
-    }
-  }
+  for (int d = 0; d < kMaxDevices; d++)
+    for (int i = 0; i < 3; i++)
+      if (t_streams.s[d][i]) {
+        cudaSetDevice(d);
+        cudaStreamSynchronize(t_streams.s[d][i]);
+        cudaStreamDestroy(t_streams.s[d][i]);
+        t_streams.s[d][i] = nullptr;
+      }
 }
 
 }  // extern "C"
