@@ -366,7 +366,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         mx[t] = fmax3(mx[t], x[e + 4], x[e + 5]);
         mx[t] = fmax3(mx[t], x[e + 6], x[e + 7]);
       }
-      const float m_new = fmaxf(m, fmax3(mx[0], mx[1], fmaxf(mx[2], mx[3])) * c_log2);
+      const float m_new = fmaxf(m, __fmul_rn(fmax3(mx[0], mx[1], fmaxf(mx[2], mx[3])), c_log2));
       float corr = 1.0f;
       bool need = false;
       if (m == -INFINITY) {
@@ -395,6 +395,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // p = 2^(s*scale*log2e - m), truncated to TF32 exactly as the tensor core
       // reads it, so the row sum l matches the P the PV MMA multiplies.
+      // The exponent argument is round(x*c) - m with both steps rounded on their
+      // own (no FMA), and m was formed as round(max x * c): the row's maximum
+      // then gives exactly 2^0.  A fused x*c - m would leave the rounding
+      // residual of x*c, which at large scores (|x*c| ~ 1e14, ulp ~ 1e7)
+      // turns 2^residual into 0 or inf.
       const float neg_m = (m == -INFINITY) ? 0.0f : -m;
       float rs[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
@@ -402,7 +407,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t rr[32];
 #pragma unroll
         for (int e = 0; e < 32; e++) {
-          const uint32_t t = __float_as_uint(ex2(fmaf(x[c * 32 + e], c_log2, neg_m))) & 0xFFFFE000u;
+          const uint32_t t = __float_as_uint(ex2(__fadd_rn(__fmul_rn(x[c * 32 + e], c_log2), neg_m))) & 0xFFFFE000u;
           rs[e & 3] += __uint_as_float(t);
           rr[e] = t;
         }
@@ -915,7 +920,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPair, 1)
       const float mx_row = fmaxf(mx_half, slot[(g ^ 1) * 128 + r]);
       // Both halves hold the same m and see the same mx_row, so they take
       // identical rescale decisions.
-      const float m_new = fmaxf(m, mx_row * c_log2);
+      const float m_new = fmaxf(m, __fmul_rn(mx_row, c_log2));
       float corr = 1.0f;
       bool need = false;
       if (m == -INFINITY) {
@@ -941,6 +946,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPair, 1)
         }
         l *= corr;
       }
+      // The exponent argument is round(x*c) - m with both steps rounded on their
+      // own (no FMA), and m was formed as round(max x * c): the row's maximum
+      // then gives exactly 2^0.  A fused x*c - m would leave the rounding
+      // residual of x*c, which at large scores (|x*c| ~ 1e14, ulp ~ 1e7)
+      // turns 2^residual into 0 or inf.
       const float neg_m = (m == -INFINITY) ? 0.0f : -m;
       float rs[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
@@ -948,7 +958,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPair, 1)
         uint32_t rr[32];
 #pragma unroll
         for (int e = 0; e < 32; e++) {
-          const uint32_t t = __float_as_uint(ex2(fmaf(x[c * 32 + e], c_log2, neg_m))) & 0xFFFFE000u;
+          const uint32_t t = __float_as_uint(ex2(__fadd_rn(__fmul_rn(x[c * 32 + e], c_log2), neg_m))) & 0xFFFFE000u;
           rs[e & 3] += __uint_as_float(t);
           rr[e] = t;
         }

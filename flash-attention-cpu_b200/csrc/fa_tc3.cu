@@ -280,7 +280,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       float mx = -INFINITY;
 #pragma unroll
       for (int e = 0; e < BK; e++) mx = fmaxf(mx, x[e]);
-      const float m_new = fmaxf(m, mx * c_log2);
+      const float m_new = fmaxf(m, __fmul_rn(mx, c_log2));
       float corr = 1.0f;
       bool need = false;
       if (m == -INFINITY) {
@@ -308,6 +308,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         l *= corr;
       }
+      // The exponent argument is round(x*c) - m with both steps rounded on their
+      // own (no FMA), and m was formed as round(max x * c): the row's maximum
+      // then gives exactly 2^0.  A fused x*c - m would leave the rounding
+      // residual of x*c, which at large scores (|x*c| ~ 1e14, ulp ~ 1e7)
+      // turns 2^residual into 0 or inf.
       const float neg_m = (m == -INFINITY) ? 0.0f : -m;
       float rs[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
@@ -315,7 +320,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t rh[32], rl[32];
 #pragma unroll
         for (int e = 0; e < 32; e++) {
-          const float pe = exp2f(fmaf(x[c * 32 + e], c_log2, neg_m));
+          const float pe = exp2f(__fadd_rn(__fmul_rn(x[c * 32 + e], c_log2), neg_m));
           const float h = hi_part(pe);
           rs[e & 3] += pe;
           rh[e] = __float_as_uint(h);
