@@ -401,19 +401,28 @@ __global__ void __launch_bounds__(kThreads, 1)
       // residual of x*c, which at large scores (|x*c| ~ 1e14, ulp ~ 1e7)
       // turns 2^residual into 0 or inf.
       const float neg_m = (m == -INFINITY) ? 0.0f : -m;
-      float rs[4] = {0.f, 0.f, 0.f, 0.f};
+      float2 rs2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+      const float2 c2 = make_float2(c_log2, c_log2), nm2 = make_float2(neg_m, neg_m);
 #pragma unroll
       for (int c = 0; c < BK / 32; c++) {
         uint32_t rr[32];
 #pragma unroll
-        for (int e = 0; e < 32; e++) {
-          const uint32_t t = __float_as_uint(ex2(__fadd_rn(__fmul_rn(x[c * 32 + e], c_log2), neg_m))) & 0xFFFFE000u;
-          rs[e & 3] += __uint_as_float(t);
-          rr[e] = t;
+        for (int e = 0; e < 32; e += 2) {
+          // packed f32x2 multiply and add (separately rounded, as for the max)
+          const float2 a = add2_rn(mul2_rn(make_float2(x[c * 32 + e], x[c * 32 + e + 1]), c2),
+                                   nm2);
+          // half of the pairs on the FMA pipe, half on MUFU
+          const float2 pe = ((e >> 1) & 1) ? ex2_poly2(a) : make_float2(ex2(a.x), ex2(a.y));
+          const uint32_t t0 = __float_as_uint(pe.x) & 0xFFFFE000u;
+          const uint32_t t1 = __float_as_uint(pe.y) & 0xFFFFE000u;
+          rs2[(e >> 1) & 1] = add2_rn(rs2[(e >> 1) & 1],
+                                      make_float2(__uint_as_float(t0), __uint_as_float(t1)));
+          rr[e] = t0;
+          rr[e + 1] = t1;
         }
         tmem_st32(t_s(b) + lane_off + c * 32, rr);
       }
-      l += (rs[0] + rs[1]) + (rs[2] + rs[3]);
+      l += (rs2[0].x + rs2[1].x) + (rs2[0].y + rs2[1].y);
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(bar_p_full(b));
@@ -952,19 +961,49 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPair, 1)
       // residual of x*c, which at large scores (|x*c| ~ 1e14, ulp ~ 1e7)
       // turns 2^residual into 0 or inf.
       const float neg_m = (m == -INFINITY) ? 0.0f : -m;
-      float rs[4] = {0.f, 0.f, 0.f, 0.f};
+      float2 rs2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+      const float2 c2 = make_float2(c_log2, c_log2), nm2 = make_float2(neg_m, neg_m);
+#ifdef FA_TRACE_SPLIT_ST
+      uint32_t pall[HC];
+#pragma unroll
+      for (int c = 0; c < HC / 32; c++) {
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          const float2 a = add2_rn(mul2_rn(make_float2(x[c * 32 + e], x[c * 32 + e + 1]), c2), nm2);
+          const uint32_t t0 = __float_as_uint(ex2(a.x)) & 0xFFFFE000u;
+          const uint32_t t1 = __float_as_uint(ex2(a.y)) & 0xFFFFE000u;
+          rs2[(e >> 1) & 1] = add2_rn(rs2[(e >> 1) & 1], make_float2(__uint_as_float(t0), __uint_as_float(t1)));
+          pall[c * 32 + e] = t0;
+          pall[c * 32 + e + 1] = t1;
+        }
+      }
+      for (int e = 0; e < HC; e++) asm volatile("" : "+r"(pall[e]));
+      if (threadIdx.x == 128 && leader) atomicAdd(&g_fa_trace[16], (unsigned long long)(clock64() - tr_a));
+#pragma unroll
+      for (int c = 0; c < HC / 32; c++)
+        tmem_st32(t_s(b) + lane_off + g * HC + c * 32, *reinterpret_cast<uint32_t(*)[32]>(pall + c * 32));
+#else
 #pragma unroll
       for (int c = 0; c < HC / 32; c++) {
         uint32_t rr[32];
 #pragma unroll
-        for (int e = 0; e < 32; e++) {
-          const uint32_t t = __float_as_uint(ex2(__fadd_rn(__fmul_rn(x[c * 32 + e], c_log2), neg_m))) & 0xFFFFE000u;
-          rs[e & 3] += __uint_as_float(t);
-          rr[e] = t;
+        for (int e = 0; e < 32; e += 2) {
+          // packed f32x2 multiply and add (separately rounded, as for the max)
+          const float2 a = add2_rn(mul2_rn(make_float2(x[c * 32 + e], x[c * 32 + e + 1]), c2),
+                                   nm2);
+          // half of the pairs on the FMA pipe, half on MUFU
+          const float2 pe = ((e >> 1) & 1) ? ex2_poly2(a) : make_float2(ex2(a.x), ex2(a.y));
+          const uint32_t t0 = __float_as_uint(pe.x) & 0xFFFFE000u;
+          const uint32_t t1 = __float_as_uint(pe.y) & 0xFFFFE000u;
+          rs2[(e >> 1) & 1] = add2_rn(rs2[(e >> 1) & 1],
+                                      make_float2(__uint_as_float(t0), __uint_as_float(t1)));
+          rr[e] = t0;
+          rr[e + 1] = t1;
         }
         tmem_st32(t_s(b) + lane_off + g * HC + c * 32, rr);
       }
-      l += (rs[0] + rs[1]) + (rs[2] + rs[3]);
+#endif
+      l += (rs2[0].x + rs2[1].x) + (rs2[0].y + rs2[1].y);
 #ifdef FA_TRACE
       if (threadIdx.x == 128 && leader) atomicAdd(&g_fa_trace[13], (unsigned long long)(clock64() - tr_a));
       tr_a = clock64();
