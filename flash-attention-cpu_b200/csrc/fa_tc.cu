@@ -918,7 +918,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPair, 1)
       const float mx_half = fmax3(mx[0], mx[1], fmaxf(mx[2], mx[3]));
       float* slot = red + (j & 1) * 256;
       slot[g * 128 + r] = mx_half;
-      if (bar_any(1, 256, !w)) {  // uniform across both warpgroups
+      // Only the two warps holding the same 32 rows (warps 4+q and 8+q, on the
+      // same scheduler) exchange halves, through named barrier 1+q; the OR makes
+      // both leave the loop together on a failure.
+      if (bar_any(1 + quarter, 64, !w)) {
         ok = false;
         break;
       }
@@ -1030,7 +1033,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPair, 1)
     // full row sum = both halves' partial sums (all 8 softmax warps reach this
     // barrier on every path: the loop above is left only uniformly)
     red[512 + g * 128 + r] = l;
-    ok = !bar_any(1, 256, !ok);
+    ok = !bar_any(1 + quarter, 64, !ok);
     const float l_row = l + red[512 + (g ^ 1) * 128 + r];
     if (ok) {
       tc_fence_after();
