@@ -1,0 +1,107 @@
+// flash_attention.hpp -- C++ mirror of the `flash-attention-cpu` crate's public
+// API (src/lib.rs:78-87) over the B200 C ABI (include/fa_b200.h).
+//
+// Same names, argument order and meaning as the crate:
+//   FlashAttentionConfig{block_size_q, block_size_kv, causal} (default 64/128/false)
+//   flash_attention_v1 / _v2 / _v3(q, k, v, seq_len_q, seq_len_k, d_head, config, out)
+//   flash_attention_multihead_v1 / _v2 / _v3(q, k, v, batch, heads, seq_len_q,
+//                                            seq_len_k, d_head, config, out)
+//   flash_attention = flash_attention_v2; flash_attention_multihead = _multihead_v2
+// Slices are std::span<const float> / std::span<float> (the crate's &[f32] /
+// &mut [f32]).  Where the crate panics -- a length mismatch, src/common.rs:51-54
+// and 87-90 -- these functions throw flash_attention_cpu::Panic with the same
+// message; a zero dimension returns without touching `out` (src/common.rs:56).
+// Every other failure (no GPU, CUDA error, bounded-wait timeout) throws
+// flash_attention_cpu::Error.  All compute runs on the GPU; there is no CPU path.
+// Link with -lfa_b200 (flash-attention-cpu_b200/lib).
+#pragma once
+
+#include <cstddef>
+#include <span>
+#include <stdexcept>
+#include <string>
+
+#include "../../include/fa_b200.h"
+
+namespace flash_attention_cpu {
+
+struct FlashAttentionConfig {
+  std::size_t block_size_q = 64;
+  std::size_t block_size_kv = 128;
+  bool causal = false;
+};
+
+class Panic : public std::logic_error {
+ public:
+  using std::logic_error::logic_error;
+};
+
+class Error : public std::runtime_error {
+ public:
+  Error(int status, const std::string& msg) : std::runtime_error(msg), status(status) {}
+  int status;
+};
+
+namespace detail {
+inline void check(int rc) {
+  if (rc == FA_OK) return;
+  const std::string msg = fa_last_error();
+  if (rc == FA_ERR_SHAPE) throw Panic(msg);
+  throw Error(rc, msg);
+}
+inline fa_config to_c(const FlashAttentionConfig& c) {
+  fa_config r;
+  r.block_size_q = c.block_size_q;
+  r.block_size_kv = c.block_size_kv;
+  r.causal = c.causal ? 1 : 0;
+  return r;
+}
+using SingleFn = int (*)(const float*, size_t, const float*, size_t, const float*, size_t, size_t,
+                         size_t, size_t, const fa_config*, float*, size_t);
+using MultiFn = int (*)(const float*, size_t, const float*, size_t, const float*, size_t, size_t,
+                        size_t, size_t, size_t, size_t, const fa_config*, float*, size_t);
+inline void single(SingleFn fn, std::span<const float> q, std::span<const float> k,
+                   std::span<const float> v, std::size_t sq, std::size_t sk, std::size_t d,
+                   const FlashAttentionConfig& cfg, std::span<float> out) {
+  const fa_config c = to_c(cfg);
+  check(fn(q.data(), q.size(), k.data(), k.size(), v.data(), v.size(), sq, sk, d, &c, out.data(),
+           out.size()));
+}
+inline void multi(MultiFn fn, std::span<const float> q, std::span<const float> k,
+                  std::span<const float> v, std::size_t batch, std::size_t heads, std::size_t sq,
+                  std::size_t sk, std::size_t d, const FlashAttentionConfig& cfg,
+                  std::span<float> out) {
+  const fa_config c = to_c(cfg);
+  check(fn(q.data(), q.size(), k.data(), k.size(), v.data(), v.size(), batch, heads, sq, sk, d,
+           &c, out.data(), out.size()));
+}
+}  // namespace detail
+
+#define FA_CPP_SINGLE(name)                                                                \
+  inline void name(std::span<const float> q, std::span<const float> k,                   \
+                   std::span<const float> v, std::size_t seq_len_q, std::size_t seq_len_k, \
+                   std::size_t d_head, const FlashAttentionConfig& config,                \
+                   std::span<float> out) {                                                \
+    detail::single(&fa_##name, q, k, v, seq_len_q, seq_len_k, d_head, config, out);       \
+  }
+FA_CPP_SINGLE(flash_attention_v1)
+FA_CPP_SINGLE(flash_attention_v2)
+FA_CPP_SINGLE(flash_attention_v3)
+FA_CPP_SINGLE(flash_attention)
+#undef FA_CPP_SINGLE
+
+#define FA_CPP_MULTI(name)                                                                   \
+  inline void name(std::span<const float> q, std::span<const float> k,                     \
+                   std::span<const float> v, std::size_t batch, std::size_t heads,          \
+                   std::size_t seq_len_q, std::size_t seq_len_k, std::size_t d_head,        \
+                   const FlashAttentionConfig& config, std::span<float> out) {              \
+    detail::multi(&fa_##name, q, k, v, batch, heads, seq_len_q, seq_len_k, d_head, config, \
+                  out);                                                                     \
+  }
+FA_CPP_MULTI(flash_attention_multihead_v1)
+FA_CPP_MULTI(flash_attention_multihead_v2)
+FA_CPP_MULTI(flash_attention_multihead_v3)
+FA_CPP_MULTI(flash_attention_multihead)
+#undef FA_CPP_MULTI
+
+}  // namespace flash_attention_cpu

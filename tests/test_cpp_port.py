@@ -1,0 +1,33 @@
+"""Builds and runs the C++ port of the crate's integration tests
+(tests/cpp/correctness_port.cpp) against the C++ API mirror.  The CPU test runs
+the cases that need no GPU (shape panics, zero-sized dimensions); the GPU test
+runs the whole port."""
+import os
+import subprocess
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+LIB = os.path.join(ROOT, "flash-attention-cpu_b200", "lib")
+ORACLE = os.path.join(ROOT, "oracle", "fa_oracle.c")
+
+
+@pytest.fixture(scope="module")
+def binary(tmp_path_factory):
+    out = str(tmp_path_factory.mktemp("cpp") / "correctness_port")
+    subprocess.run(["g++", "-std=c++20", "-O2", "-o", out,
+                    os.path.join(ROOT, "tests", "cpp", "correctness_port.cpp"), "-x", "c",
+                    ORACLE, "-x", "none", f"-L{LIB}", "-lfa_b200", f"-Wl,-rpath,{LIB}",
+                    "-lm", "-lpthread"], check=True)
+    return out
+
+
+def test_cpp_port_cpu_cases(binary):
+    r = subprocess.run([binary, "cpu"], capture_output=True, text=True)
+    assert r.returncode == 0, r.stdout + r.stderr
+
+
+@pytest.mark.gpu
+def test_cpp_port_all_cases(binary, gpu_lib):
+    r = subprocess.run([binary], capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stdout + r.stderr
