@@ -602,7 +602,7 @@ struct PairCfg {
   static constexpr int kOffBar = kOffV + NVS * kVBytes;
   static constexpr int kNumBars = 1 + 2 * NKS + 2 * NVS + 2 + 2 + 3;
   static constexpr int kOffRed = (kOffBar + kNumBars * 8 + 16 + 15) / 16 * 16;
-  static constexpr int kSmemBytes = kOffRed + 3 * 2 * 128 * 4 + 1024;
+  static constexpr int kSmemBytes = kOffRed + 4 * 2 * 128 * 4 + 1024;
   static constexpr int kTmemColsUsed = 2 * D + 2 * BK;
   static constexpr int kTmemCols = kTmemColsUsed <= 256 ? 256 : 512;
   static_assert(D % 64 == 0 && D <= 128, "pair kernel: D in {64, 128}");
@@ -616,14 +616,18 @@ constexpr int kThreadsPair = 384;  // 12 warps: 2 producers, MMA, idle, 2 softma
 template <int D, int BK, int NKS, int NVS>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPair, 1)
     tc_fwd_tf32_pair(const __grid_constant__ CUtensorMap tmK,
-                     const __grid_constant__ CUtensorMap tmV, FwdParams p) {
+                     const __grid_constant__ CUtensorMap tmV, FwdParams p, int n_pairs) {
+  // Persistent: cluster c computes work tiles w = c, c + C, ... (C clusters),
+  // each tile = 256 query rows (a pair) of one slice, heaviest causal tiles
+  // first.  Every ring and buffer index continues across tiles through the
+  // global key-block counter G, so the producers run ahead into the next tile
+  // while the current one finishes; the softmax warps stage the next tile's Q
+  // before writing out the current tile's O, so QK^T of the next tile overlaps
+  // that epilogue.
   using C = PairCfg<D, BK, NKS, NVS>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
-#ifdef FA_TRACE
-  const long long tr_kstart = clock64();
-#endif
   const uint32_t rank = cluster_rank();
   const bool leader = rank == 0;
   const uint32_t sbase = smem_u32(smem);
@@ -638,26 +642,44 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPair, 1)
   constexpr uint32_t kB2 = 1 + 2 * NKS + 2 * NVS;
   auto bar_s_full = [&](int b) { return bar0 + 8u * (kB2 + b); };
   auto bar_p_full = [&](int b) { return bar0 + 8u * (kB2 + 2 + b); };
+  // o_done completes once per PV (global order).  A wait on it for PV(G-1) at
+  // softmax block G is unambiguous: S(G) was issued after PV(G-2), so when S(G)
+  // is visible at most PV(G-1) and PV(G) remain, and PV(G) needs P(G).
   const uint32_t bar_o_done = bar0 + 8u * (kB2 + 4);
   const uint32_t bar_drain = bar0 + 8u * (kB2 + 5);
+  // o_final completes once per work tile (its last PV, or at once for a tile
+  // that sees no key).  The next tile's first PV needs P of its first block,
+  // which its softmax produces only after the previous tile's O was read out,
+  // so no separate "O free" barrier is needed.
   const uint32_t bar_o_final = bar0 + 8u * (kB2 + 6);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kOffBar + C::kNumBars * 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  // the same barrier in the leader's / the peer's shared memory (cluster addresses)
   auto at_leader = [&](uint32_t bar) { return map_to_rank(bar, 0); };
   auto at_peer = [&](uint32_t bar) { return map_to_rank(bar, 1); };
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int bh = blockIdx.y;
-  const int n_pairs = gridDim.z;
-  const int pair = n_pairs - 1 - (int)blockIdx.z;  // heaviest causal pairs dispatched first
-  const int q0_pair = pair * 2 * kBM;
-  const int q0 = q0_pair + (int)rank * kBM;        // this CTA's first row
-  const int q_rows = max(0, min(kBM, p.sq - q0));
-  const int pair_rows = min(2 * kBM, p.sq - q0_pair);
-  int kend = p.sk;
-  if (p.causal) kend = causal_limit(p.q_offset + q0_pair + pair_rows - 1, p.k_offset, p.sk);
-  const int n_kv = (kend + BK - 1) / BK;
+  const int cid = (int)(blockIdx.x >> 1), n_clusters = (int)(gridDim.x >> 1);
+  const int n_work = n_pairs * p.bh;
+  struct Tile {
+    int bh, q0_pair, q0, q_rows, n_kv;
+  };
+  // Round k of the static schedule: tiles k*C .. k*C+C-1 (heaviest first),
+  // dealt in snake order (reversed on odd rounds) so that every cluster's
+  // total causal work comes out nearly equal.
+  auto work_of = [&](int k) { return k * n_clusters + ((k & 1) ? n_clusters - 1 - cid : cid); };
+  auto tile_of = [&](int w) {
+    Tile t;
+    const int pair = n_pairs - 1 - w / p.bh;  // heaviest causal pairs first
+    t.bh = w % p.bh;
+    t.q0_pair = pair * 2 * kBM;
+    t.q0 = t.q0_pair + (int)rank * kBM;
+    t.q_rows = max(0, min(kBM, p.sq - t.q0));
+    const int pair_rows = min(2 * kBM, p.sq - t.q0_pair);
+    int kend = p.sk;
+    if (p.causal) kend = causal_limit(p.q_offset + t.q0_pair + pair_rows - 1, p.k_offset, p.sk);
+    t.n_kv = (kend + BK - 1) / BK;
+    return t;
+  };
 
   if (threadIdx.x == 0) {
     mbar_init(bar_q_full, 16);  // 8 softmax warps x 2 CTAs
@@ -693,68 +715,52 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPair, 1)
   const uint32_t t_q = tmem;
   const uint32_t t_o = tmem + (uint32_t)D;
   auto t_s = [&](int b) { return tmem + (uint32_t)(2 * D + b * BK); };
-  // Either CTA's earlier failure skips the work of both (the flag is global).
   const bool skip = *abort_flag != 0;
 
-  if (warp == 0) {
-    // ------------------------------ K producer: this CTA's 64-key half of each tile
+  if (warp == 0 || warp == 2) {
+    // ------------------------------ TMA producers: warp 0 K halves, warp 2 V halves
+    const bool is_k = warp == 0;
+    const int NS = is_k ? NKS : NVS;
     if (lane == 0 && !skip) {
-      int issued = 0;
+      int G = 0;  // global key-block counter
       bool ok = true;
-      for (int j = 0; j < n_kv && ok; j++) {
-        const int sk = j % NKS;
-        {
-          FA_TR_T0();
-          if (j >= NKS) ok = mbar_wait(bar_k_empty(sk), ((j / NKS) & 1) ^ 1, abort_flag, p.err);
-          if (leader) FA_TR_ADD(0);
+      for (int k = 0; k * n_clusters < n_work && ok; k++) {
+        const int w = work_of(k);
+        if (w >= n_work) continue;
+        const Tile t = tile_of(w);
+        for (int j = 0; j < t.n_kv && ok; j++, G++) {
+          const int s = G % NS;
+          if (G >= NS)
+            ok = mbar_wait(is_k ? bar_k_empty(s) : bar_v_empty(s), ((G / NS) & 1) ^ 1, abort_flag,
+                           p.err);
+          if (!ok) break;
+          const uint32_t full = at_leader(is_k ? bar_k_full(s) : bar_v_full(s));
+          if (is_k) {
+            mbar_expect_tx_cluster(full, C::kKBytes);
+            for (int c = 0; c < D / 32; c++)
+              tma_load_3d_pair(sK + s * C::kKBytes + c * C::kKHalf * 128, &tmK, full, 32 * c,
+                               j * BK + (int)rank * C::kKHalf, t.bh);
+          } else {
+            mbar_expect_tx_cluster(full, C::kVBytes);
+            for (int c = 0; c < C::kDHalf / 32; c++)
+              tma_load_3d_pair(sV + s * C::kVBytes + c * BK * 128, &tmV, full,
+                               (int)rank * C::kDHalf + 32 * c, j * BK, t.bh);
+          }
         }
-        if (!ok) break;
-        FA_EV(8, j);
-        const uint32_t full = at_leader(bar_k_full(sk));
-        mbar_expect_tx_cluster(full, C::kKBytes);
-        for (int c = 0; c < D / 32; c++)
-          tma_load_3d_pair(sK + sk * C::kKBytes + c * C::kKHalf * 128, &tmK, full, 32 * c,
-                           j * BK + (int)rank * C::kKHalf, bh);
-        issued = j + 1;
       }
+      // Wait (bounded, ignoring the abort flag) for the last load of every slot
+      // (the leader's barriers count both CTAs' bytes), so no TMA write can
+      // land after the CTAs exit even when a consumer role aborted.
       volatile int no_abort = 0;
       if (leader)
-        for (int j = max(0, issued - NKS); j < issued; j++)
-          mbar_wait(bar_k_full(j % NKS), (j / NKS) & 1, &no_abort, p.err);
-    }
-    __syncwarp();
-  } else if (warp == 2) {
-    // ------------------------------ V producer: all BK keys x this CTA's D/2 columns
-    if (lane == 0 && !skip) {
-      int issued = 0;
-      bool ok = true;
-      for (int j = 0; j < n_kv && ok; j++) {
-        const int sv = j % NVS;
-        {
-          FA_TR_T0();
-          if (j >= NVS) ok = mbar_wait(bar_v_empty(sv), ((j / NVS) & 1) ^ 1, abort_flag, p.err);
-          if (leader) FA_TR_ADD(1);
-        }
-        if (!ok) break;
-        FA_EV(9, j);
-        const uint32_t full = at_leader(bar_v_full(sv));
-        mbar_expect_tx_cluster(full, C::kVBytes);
-        for (int c = 0; c < C::kDHalf / 32; c++)
-          tma_load_3d_pair(sV + sv * C::kVBytes + c * BK * 128, &tmV, full,
-                           (int)rank * C::kDHalf + 32 * c, j * BK, bh);
-        issued = j + 1;
-      }
-      volatile int no_abort = 0;
-      if (leader)
-        for (int j = max(0, issued - NVS); j < issued; j++)
-          mbar_wait(bar_v_full(j % NVS), (j / NVS) & 1, &no_abort, p.err);
+        for (int g = max(0, G - NS); g < G; g++)
+          mbar_wait(is_k ? bar_k_full(g % NS) : bar_v_full(g % NS), (g / NS) & 1, &no_abort,
+                    p.err);
     }
     __syncwarp();
   } else if (warp == 1) {
-    // ------------------------------ MMA issuer (leader CTA only)
-    // The whole warp runs this loop so descriptors and addresses stay
-    // warp-uniform (uniform registers); one elected lane issues each
-    // tcgen05.mma / tcgen05.commit.
+    // ------------------------------ MMA issuer (leader CTA only; warp-uniform, one
+    // elected lane issues each tcgen05.mma / tcgen05.commit)
     if (leader && !skip) {
       constexpr uint32_t idesc_qk = instr_desc(2 * kBM, BK, false);
       constexpr uint32_t idesc_pv = instr_desc(2 * kBM, D, true);
@@ -762,77 +768,70 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPair, 1)
         tc_commit_pair_elect(bar);           // this CTA's copy
         tc_commit_pair_elect(at_peer(bar));  // the peer's copy
       };
-      bool ok = __all_sync(0xffffffffu, mbar_wait(bar_q_full, 0, abort_flag, p.err));
-      tc_fence_after();
-      auto issue_pv = [&](int jj) -> bool {
-        const int b = jj & 1, sv = jj % NVS;
-        {
-          FA_TR_T0();
-          if (!__all_sync(0xffffffffu, mbar_wait(bar_p_full(b), (jj >> 1) & 1, abort_flag, p.err)))
-            return false;
-          if (lane == 0) FA_TR_ADD(3);
-          FA_EV(2, jj);
-        }
-        {
-          FA_TR_T0();
-          if (!__all_sync(0xffffffffu, mbar_wait(bar_v_full(sv), (jj / NVS) & 1, abort_flag, p.err)))
-            return false;
-          if (lane == 0) FA_TR_ADD(4);
-          FA_EV(10, jj);
-        }
+      // PV of global block G (block j of its tile): O (+)= P(G) V(G)
+      auto issue_pv = [&](int G, int j) -> bool {
+        const int b = G & 1, sv = G % NVS;
+        if (!__all_sync(0xffffffffu, mbar_wait(bar_p_full(b), (G >> 1) & 1, abort_flag, p.err)))
+          return false;
+        if (!__all_sync(0xffffffffu, mbar_wait(bar_v_full(sv), (G / NVS) & 1, abort_flag, p.err)))
+          return false;
         tc_fence_after();
         // 8 keys per MMA = two 4-row groups (SBO = 512 B); 32-column chunks LBO apart
         const uint64_t vdesc = smem_desc(sV + sv * C::kVBytes, BK * 128, 512, kLayoutSw128Base32);
 #pragma unroll
         for (int kk = 0; kk < BK / 8; kk++)
           mma_ts_pair_elect(t_o, t_s(b) + kk * 8, vdesc + (uint64_t)(kk * 64), idesc_pv,
-                            (jj > 0 || kk > 0) ? 1u : 0u);
+                            (j > 0 || kk > 0) ? 1u : 0u);
         commit_both(bar_v_empty(sv));
         commit_both(bar_o_done);
-        FA_EV(3, jj);
         return true;
       };
-      for (int j = 0; j < n_kv && ok; j++) {
-        const int s = j % NKS, b = j & 1;
-        {
-          FA_TR_T0();
-          ok = __all_sync(0xffffffffu, mbar_wait(bar_k_full(s), (j / NKS) & 1, abort_flag, p.err));
-          if (lane == 0) FA_TR_ADD(2);
-          FA_EV(0, j);
-        }
+      bool ok = true;
+      int G = 0, it = 0;
+      for (int k = 0; k * n_clusters < n_work && ok; k++) {
+        const int w = work_of(k);
+        if (w >= n_work) continue;
+        const Tile t = tile_of(w);
+        ok = __all_sync(0xffffffffu, mbar_wait(bar_q_full, it & 1, abort_flag, p.err));
         if (!ok) break;
         tc_fence_after();
-        const uint64_t kdesc = smem_desc(sK + s * C::kKBytes, 16, 1024, kLayoutSw128);
+        for (int j = 0; j < t.n_kv && ok; j++) {
+          const int Gj = G + j, s = Gj % NKS, b = Gj & 1;
+          ok = __all_sync(0xffffffffu, mbar_wait(bar_k_full(s), (Gj / NKS) & 1, abort_flag, p.err));
+          if (!ok) break;
+          tc_fence_after();
+          const uint64_t kdesc = smem_desc(sK + s * C::kKBytes, 16, 1024, kLayoutSw128);
 #pragma unroll
-        for (int kk = 0; kk < D / 8; kk++)
-          mma_ts_pair_elect(t_s(b), t_q + kk * 8,
-                            kdesc + (uint64_t)(((kk >> 2) * C::kKHalf * 128 + (kk & 3) * 32) >> 4),
-                            idesc_qk, kk > 0 ? 1u : 0u);
-        commit_both(bar_s_full(b));
-        commit_both(bar_k_empty(s));
-        FA_EV(1, j);
-        if (j > 0) ok = issue_pv(j - 1);
+          for (int kk = 0; kk < D / 8; kk++)
+            mma_ts_pair_elect(t_s(b), t_q + kk * 8,
+                              kdesc + (uint64_t)(((kk >> 2) * C::kKHalf * 128 + (kk & 3) * 32) >> 4),
+                              idesc_qk, kk > 0 ? 1u : 0u);
+          commit_both(bar_s_full(b));
+          commit_both(bar_k_empty(s));
+          if (j > 0) ok = issue_pv(Gj - 1, j - 1);
+        }
+        if (ok && t.n_kv > 0) ok = issue_pv(G + t.n_kv - 1, t.n_kv - 1);
+        if (!ok) break;
+        commit_both(bar_o_final);  // (at once for a tile with no key block)
+        G += t.n_kv;
+        it++;
       }
-      if (ok && n_kv > 0 && issue_pv(n_kv - 1)) commit_both(bar_o_final);
       commit_both(bar_drain);
     }
     __syncwarp();
   } else if (warp >= kSoftmaxWarp0) {
     // ------------------------------ softmax: two warpgroups, thread = (row, half)
     // Warpgroup g (warps 4-7: g = 0, warps 8-11: g = 1) handles columns
-    // [g*BK/2, (g+1)*BK/2) of every score row and O columns [g*D/2, (g+1)*D/2):
-    // two warps per scheduler hide each other's latency.  The two halves of a
-    // row exchange their partial maxima once per tile through shared memory;
-    // each keeps its own partial row sum until the epilogue.
+    // [g*BK/2, (g+1)*BK/2) of every score row and O columns [g*D/2, (g+1)*D/2);
+    // the two halves of a row exchange partial maxima once per block through
+    // shared memory and keep separate partial row sums until the epilogue.
     constexpr int HC = BK / 2, HD = D / 2;
     const int g = (warp - kSoftmaxWarp0) >> 2;
     const int quarter = warp & 3;  // TMEM lanes 32*quarter..
     const int r = quarter * 32 + lane;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-    const long long qg = p.q_offset + q0 + r;
     const float c_log2 = p.scale_log2;
-    float* red = reinterpret_cast<float*>(smem + C::kOffRed);  // [3][2][128]
-    bool ok = !skip;
+    float* red = reinterpret_cast<float*>(smem + C::kOffRed);  // [4][2][128]
     auto warp_arrive_leader = [&](uint32_t bar) {
       __syncwarp();
       if (lane == 0) {
@@ -842,228 +841,205 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPair, 1)
           mbar_arrive_remote(at_leader(bar));
       }
     };
-    if (ok) {
-      const bool valid = r < q_rows;
-      const float4* qrow =
-          reinterpret_cast<const float4*>(p.q + ((size_t)bh * p.sq + q0 + r) * D + g * HD);
-#pragma unroll
-      for (int c = 0; c < HD / 32; c++) {
-        uint32_t rr[32];
-#pragma unroll
-        for (int e = 0; e < 8; e++) {
-          const float4 v4 = valid ? __ldg(qrow + c * 8 + e) : make_float4(0.f, 0.f, 0.f, 0.f);
-          rr[4 * e + 0] = to_tf32_rna(v4.x);
-          rr[4 * e + 1] = to_tf32_rna(v4.y);
-          rr[4 * e + 2] = to_tf32_rna(v4.z);
-          rr[4 * e + 3] = to_tf32_rna(v4.w);
-        }
-        tmem_st32(t_q + lane_off + g * HD + c * 32, rr);
-      }
-      tmem_wait_st();
-      tc_fence_before();
-      warp_arrive_leader(bar_q_full);
-    }
-    float m = -INFINITY, l = 0.0f;  // l: this half's partial row sum
-    for (int j = 0; j < n_kv && ok; j++) {
-      const int b = j & 1;
-      bool w;
-      {
-        FA_TR_T0();
-        w = __all_sync(0xffffffffu, mbar_wait(bar_s_full(b), (j >> 1) & 1, abort_flag, p.err));
-        if (threadIdx.x == 128 && leader) FA_TR_ADD(5);
-        if (threadIdx.x == 128) FA_EV(4, j);
-        if (threadIdx.x == 256) FA_EV(6, j);
-      }
-      FA_TR_T0();
-      tc_fence_after();
-      float x[HC];
-#ifdef FA_TRACE
-      long long tr_a = clock64();
-#endif
-      if (w) {
-        uint32_t sr[HC];
-#pragma unroll
-        for (int c = 0; c < HC / 32; c++)
-          tmem_ld32(t_s(b) + lane_off + g * HC + c * 32,
-                    *reinterpret_cast<uint32_t(*)[32]>(sr + c * 32));
-        tmem_wait_ld_regs(sr);
-#ifdef FA_TRACE
-        if (threadIdx.x == 128 && leader) atomicAdd(&g_fa_trace[11], (unsigned long long)(clock64() - tr_a));
-        tr_a = clock64();
-#endif
-#pragma unroll
-        for (int e = 0; e < HC; e++) x[e] = __uint_as_float(sr[e]);
-      } else {
-#pragma unroll
-        for (int e = 0; e < HC; e++) x[e] = -INFINITY;
-      }
-      const int kbase = j * BK + g * HC;
-      int lim = min(HC, p.sk - kbase);
-      if (p.causal) lim = min(lim, causal_limit(qg, p.k_offset + kbase, HC));
-      if (!__all_sync(0xffffffffu, lim == HC)) {
-#pragma unroll
-        for (int e = 0; e < HC; e++) x[e] = (e < lim) ? x[e] : -INFINITY;
-      }
-      float mx[4];
-#pragma unroll
-      for (int t = 0; t < 4; t++) mx[t] = -INFINITY;
-#pragma unroll
-      for (int e = 0; e < HC; e += 8) {
-        const int t = (e >> 3) & 3;
-        mx[t] = fmax3(mx[t], x[e], x[e + 1]);
-        mx[t] = fmax3(mx[t], x[e + 2], x[e + 3]);
-        mx[t] = fmax3(mx[t], x[e + 4], x[e + 5]);
-        mx[t] = fmax3(mx[t], x[e + 6], x[e + 7]);
-      }
-      const float mx_half = fmax3(mx[0], mx[1], fmaxf(mx[2], mx[3]));
-      float* slot = red + (j & 1) * 256;
-      slot[g * 128 + r] = mx_half;
-      // Only the two warps holding the same 32 rows (warps 4+q and 8+q, on the
-      // same scheduler) exchange halves, through named barrier 1+q; the OR makes
-      // both leave the loop together on a failure.
-      if (bar_any(1 + quarter, 64, !w)) {
-        ok = false;
-        break;
-      }
-#ifdef FA_TRACE
-      if (threadIdx.x == 128 && leader) atomicAdd(&g_fa_trace[12], (unsigned long long)(clock64() - tr_a));
-      tr_a = clock64();
-#endif
-      const float mx_row = fmaxf(mx_half, slot[(g ^ 1) * 128 + r]);
-      // Both halves hold the same m and see the same mx_row, so they take
-      // identical rescale decisions.
-      const float m_new = fmaxf(m, __fmul_rn(mx_row, c_log2));
-      float corr = 1.0f;
-      bool need = false;
-      if (m == -INFINITY) {
-        m = m_new;
-      } else if (m_new > m + kRescaleLog2) {
-        need = true;
-        corr = ex2(m - m_new);
-        m = m_new;
-      }
-      if (__any_sync(0xffffffffu, need) &&
-          __all_sync(0xffffffffu, mbar_wait(bar_o_done, (j - 1) & 1, abort_flag, p.err))) {
-        // (a failed wait raises the abort flag; the loop then ends at the
-        // next tile's bar_any)
+    bool ok = !skip;
+    // state of the previous tile, written out after the next tile's Q is staged
+    bool have_prev = false;
+    Tile pt{};
+    int pit = 0;
+    float pm = -INFINITY, pl = 0.0f;
+    auto epilogue = [&]() {
+      // all 8 softmax warps of the quarter pair reach this on every path
+      bool w = ok;
+      if (w) w = __all_sync(0xffffffffu, mbar_wait(bar_o_final, pit & 1, abort_flag, p.err));
+      if (*abort_flag) w = false;
+      // row-sum exchange slot alternates by tile, so a slot is rewritten only
+      // after both warps have passed the next epilogue's barrier
+      float* lslot = red + 512 + (pit & 1) * 256;
+      lslot[g * 128 + r] = pl;
+      ok = !bar_any(1 + quarter, 64, !w);
+      const float l_row = pl + lslot[(g ^ 1) * 128 + r];
+      if (ok) {
         tc_fence_after();
+        const float inv_l = l_row > 0.0f ? 1.0f / l_row : 0.0f;
+        const bool row_ok = r < pt.q_rows;
+        float* orow = p.o + ((size_t)pt.bh * p.sq + pt.q0 + r) * D + g * HD;
 #pragma unroll
         for (int c = 0; c < HD / 32; c++) {
           uint32_t rr[32];
-          tmem_ld32(t_o + lane_off + g * HD + c * 32, rr);
-          tmem_wait_ld_regs(rr);
+          if (pt.n_kv > 0) {
+            tmem_ld32(t_o + lane_off + g * HD + c * 32, rr);
+            tmem_wait_ld_regs(rr);
+          } else {
 #pragma unroll
-          for (int e = 0; e < 32; e++) rr[e] = __float_as_uint(__uint_as_float(rr[e]) * corr);
-          tmem_st32(t_o + lane_off + g * HD + c * 32, rr);
-        }
-        l *= corr;
-      }
-      // The exponent argument is round(x*c) - m with both steps rounded on their
-      // own (no FMA), and m was formed as round(max x * c): the row's maximum
-      // then gives exactly 2^0.  A fused x*c - m would leave the rounding
-      // residual of x*c, which at large scores (|x*c| ~ 1e14, ulp ~ 1e7)
-      // turns 2^residual into 0 or inf.
-      const float neg_m = (m == -INFINITY) ? 0.0f : -m;
-      float2 rs2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
-      const float2 c2 = make_float2(c_log2, c_log2), nm2 = make_float2(neg_m, neg_m);
-#ifdef FA_TRACE_SPLIT_ST
-      uint32_t pall[HC];
+            for (int e = 0; e < 32; e++) rr[e] = 0u;
+          }
+          if (row_ok) {
 #pragma unroll
-      for (int c = 0; c < HC / 32; c++) {
-#pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          const float2 a = add2_rn(mul2_rn(make_float2(x[c * 32 + e], x[c * 32 + e + 1]), c2), nm2);
-          const uint32_t t0 = __float_as_uint(ex2(a.x)) & 0xFFFFE000u;
-          const uint32_t t1 = __float_as_uint(ex2(a.y)) & 0xFFFFE000u;
-          rs2[(e >> 1) & 1] = add2_rn(rs2[(e >> 1) & 1], make_float2(__uint_as_float(t0), __uint_as_float(t1)));
-          pall[c * 32 + e] = t0;
-          pall[c * 32 + e + 1] = t1;
-        }
-      }
-      for (int e = 0; e < HC; e++) asm volatile("" : "+r"(pall[e]));
-      if (threadIdx.x == 128 && leader) atomicAdd(&g_fa_trace[16], (unsigned long long)(clock64() - tr_a));
-#pragma unroll
-      for (int c = 0; c < HC / 32; c++)
-        tmem_st32(t_s(b) + lane_off + g * HC + c * 32, *reinterpret_cast<uint32_t(*)[32]>(pall + c * 32));
-#else
-#pragma unroll
-      for (int c = 0; c < HC / 32; c++) {
-        uint32_t rr[32];
-#pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          // packed f32x2 multiply and add (separately rounded, as for the max)
-          const float2 a = add2_rn(mul2_rn(make_float2(x[c * 32 + e], x[c * 32 + e + 1]), c2),
-                                   nm2);
-          // half of the pairs on the FMA pipe, half on MUFU
-          const float2 pe = ((e >> 1) & 1) ? ex2_poly2(a) : make_float2(ex2(a.x), ex2(a.y));
-          const uint32_t t0 = __float_as_uint(pe.x) & 0xFFFFE000u;
-          const uint32_t t1 = __float_as_uint(pe.y) & 0xFFFFE000u;
-          rs2[(e >> 1) & 1] = add2_rn(rs2[(e >> 1) & 1],
-                                      make_float2(__uint_as_float(t0), __uint_as_float(t1)));
-          rr[e] = t0;
-          rr[e + 1] = t1;
-        }
-        tmem_st32(t_s(b) + lane_off + g * HC + c * 32, rr);
-      }
-#endif
-      l += (rs2[0].x + rs2[1].x) + (rs2[0].y + rs2[1].y);
-#ifdef FA_TRACE
-      if (threadIdx.x == 128 && leader) atomicAdd(&g_fa_trace[13], (unsigned long long)(clock64() - tr_a));
-      tr_a = clock64();
-#endif
-      tmem_wait_st();
-#ifdef FA_TRACE
-      if (threadIdx.x == 128 && leader) atomicAdd(&g_fa_trace[14], (unsigned long long)(clock64() - tr_a));
-      tr_a = clock64();
-#endif
-      tc_fence_before();
-      warp_arrive_leader(bar_p_full(b));
-#ifdef FA_TRACE
-      if (threadIdx.x == 128 && leader) atomicAdd(&g_fa_trace[15], (unsigned long long)(clock64() - tr_a));
-#endif
-      if (threadIdx.x == 128) FA_EV(5, j);
-      if (threadIdx.x == 256) FA_EV(7, j);
-      if (threadIdx.x == 128 && leader) {
-        FA_TR_ADD(6);
-        FA_TR_CNT(8);
-      }
-    }
-    if (n_kv > 0 && ok) ok = __all_sync(0xffffffffu, mbar_wait(bar_o_final, 0, abort_flag, p.err));
-    if (*abort_flag) ok = false;
-    // full row sum = both halves' partial sums (all 8 softmax warps reach this
-    // barrier on every path: the loop above is left only uniformly)
-    red[512 + g * 128 + r] = l;
-    ok = !bar_any(1 + quarter, 64, !ok);
-    const float l_row = l + red[512 + (g ^ 1) * 128 + r];
-    if (ok) {
-      tc_fence_after();
-      const float inv_l = l_row > 0.0f ? 1.0f / l_row : 0.0f;
-      const bool row_ok = r < q_rows;
-      float* orow = p.o + ((size_t)bh * p.sq + q0 + r) * D + g * HD;
-#pragma unroll
-      for (int c = 0; c < HD / 32; c++) {
-        uint32_t rr[32];
-        if (n_kv > 0) {
-          tmem_ld32(t_o + lane_off + g * HD + c * 32, rr);
-          tmem_wait_ld_regs(rr);
-        } else {
-#pragma unroll
-          for (int e = 0; e < 32; e++) rr[e] = 0u;
-        }
-        if (row_ok) {
-#pragma unroll
-          for (int e = 0; e < 32; e += 4) {
-            float4 v4 = make_float4(__uint_as_float(rr[e]) * inv_l, __uint_as_float(rr[e + 1]) * inv_l,
-                                    __uint_as_float(rr[e + 2]) * inv_l,
-                                    __uint_as_float(rr[e + 3]) * inv_l);
-            *reinterpret_cast<float4*>(orow + c * 32 + e) = v4;
+            for (int e = 0; e < 32; e += 4) {
+              float4 v4 =
+                  make_float4(__uint_as_float(rr[e]) * inv_l, __uint_as_float(rr[e + 1]) * inv_l,
+                              __uint_as_float(rr[e + 2]) * inv_l, __uint_as_float(rr[e + 3]) * inv_l);
+              *reinterpret_cast<float4*>(orow + c * 32 + e) = v4;
+            }
           }
         }
+        if (row_ok && g == 0 && p.lse)
+          p.lse[(size_t)pt.bh * p.sq + pt.q0 + r] =
+              l_row > 0.0f ? (pm + __log2f(l_row)) * 0.69314718055994530942f : -INFINITY;
+        tc_fence_before();  // O reads done before this thread's next barrier arrive
       }
-      if (row_ok && g == 0 && p.lse)
-        p.lse[(size_t)bh * p.sq + q0 + r] =
-            l_row > 0.0f ? (m + __log2f(l_row)) * 0.69314718055994530942f : -INFINITY;
+    };
+    int G = 0, it = 0;
+    for (int k = 0; k * n_clusters < n_work && ok; k++) {
+      const int w = work_of(k);
+      if (w >= n_work) continue;
+      const Tile t = tile_of(w);
+      const long long qg = p.q_offset + t.q0 + r;
+      {
+        // Stage this tile's Q.  The previous tile's QK^T MMAs are complete: its
+        // last S was visible before its last P was written.
+        const bool valid = r < t.q_rows;
+        const float4* qrow = reinterpret_cast<const float4*>(
+            p.q + ((size_t)t.bh * p.sq + t.q0 + r) * D + g * HD);
+#pragma unroll
+        for (int c = 0; c < HD / 32; c++) {
+          uint32_t rr[32];
+#pragma unroll
+          for (int e = 0; e < 8; e++) {
+            const float4 v4 = valid ? __ldg(qrow + c * 8 + e) : make_float4(0.f, 0.f, 0.f, 0.f);
+            rr[4 * e + 0] = to_tf32_rna(v4.x);
+            rr[4 * e + 1] = to_tf32_rna(v4.y);
+            rr[4 * e + 2] = to_tf32_rna(v4.z);
+            rr[4 * e + 3] = to_tf32_rna(v4.w);
+          }
+          tmem_st32(t_q + lane_off + g * HD + c * 32, rr);
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        warp_arrive_leader(bar_q_full);
+      }
+      if (have_prev) {
+        epilogue();
+        if (!ok) break;
+      }
+      float m = -INFINITY, l = 0.0f;  // l: this half's partial row sum
+      for (int j = 0; j < t.n_kv && ok; j++) {
+        const int Gj = G + j, b = Gj & 1;
+        const bool wt =
+            __all_sync(0xffffffffu, mbar_wait(bar_s_full(b), (Gj >> 1) & 1, abort_flag, p.err));
+        tc_fence_after();
+        float x[HC];
+        if (wt) {
+          uint32_t sr[HC];
+#pragma unroll
+          for (int c = 0; c < HC / 32; c++)
+            tmem_ld32(t_s(b) + lane_off + g * HC + c * 32,
+                      *reinterpret_cast<uint32_t(*)[32]>(sr + c * 32));
+          tmem_wait_ld_regs(sr);
+#pragma unroll
+          for (int e = 0; e < HC; e++) x[e] = __uint_as_float(sr[e]);
+        } else {
+#pragma unroll
+          for (int e = 0; e < HC; e++) x[e] = -INFINITY;
+        }
+        const int kbase = j * BK + g * HC;
+        int lim = min(HC, p.sk - kbase);
+        if (p.causal) lim = min(lim, causal_limit(qg, p.k_offset + kbase, HC));
+        if (!__all_sync(0xffffffffu, lim == HC)) {
+#pragma unroll
+          for (int e = 0; e < HC; e++) x[e] = (e < lim) ? x[e] : -INFINITY;
+        }
+        float mx[4];
+#pragma unroll
+        for (int q = 0; q < 4; q++) mx[q] = -INFINITY;
+#pragma unroll
+        for (int e = 0; e < HC; e += 8) {
+          const int q = (e >> 3) & 3;
+          mx[q] = fmax3(mx[q], x[e], x[e + 1]);
+          mx[q] = fmax3(mx[q], x[e + 2], x[e + 3]);
+          mx[q] = fmax3(mx[q], x[e + 4], x[e + 5]);
+          mx[q] = fmax3(mx[q], x[e + 6], x[e + 7]);
+        }
+        const float mx_half = fmax3(mx[0], mx[1], fmaxf(mx[2], mx[3]));
+        float* slot = red + (Gj & 1) * 256;
+        slot[g * 128 + r] = mx_half;
+        // Only the two warps holding the same 32 rows (warps 4+q and 8+q, on the
+        // same scheduler) exchange halves, through named barrier 1+q; the OR makes
+        // both leave the loop together on a failure.
+        if (bar_any(1 + quarter, 64, !wt)) {
+          ok = false;
+          break;
+        }
+        const float mx_row = fmaxf(mx_half, slot[(g ^ 1) * 128 + r]);
+        // Both halves hold the same m and see the same mx_row, so they take
+        // identical rescale decisions.
+        const float m_new = fmaxf(m, __fmul_rn(mx_row, c_log2));
+        float corr = 1.0f;
+        bool need = false;
+        if (m == -INFINITY) {
+          m = m_new;
+        } else if (m_new > m + kRescaleLog2) {
+          need = true;
+          corr = ex2(m - m_new);
+          m = m_new;
+        }
+        if (__any_sync(0xffffffffu, need) &&
+            __all_sync(0xffffffffu, mbar_wait(bar_o_done, (Gj - 1) & 1, abort_flag, p.err))) {
+          // (a failed wait raises the abort flag; the loop then ends at the
+          // next block's bar_any)
+          tc_fence_after();
+#pragma unroll
+          for (int c = 0; c < HD / 32; c++) {
+            uint32_t rr[32];
+            tmem_ld32(t_o + lane_off + g * HD + c * 32, rr);
+            tmem_wait_ld_regs(rr);
+#pragma unroll
+            for (int e = 0; e < 32; e++) rr[e] = __float_as_uint(__uint_as_float(rr[e]) * corr);
+            tmem_st32(t_o + lane_off + g * HD + c * 32, rr);
+          }
+          l *= corr;
+        }
+        // The exponent argument is round(x*c) - m with both steps rounded on
+        // their own (no FMA), and m was formed as round(max x * c): the row's
+        // maximum then gives exactly 2^0.  A fused x*c - m would leave the
+        // rounding residual of x*c, which at large scores (|x*c| ~ 1e14, ulp
+        // ~ 1e7) turns 2^residual into 0 or inf.
+        const float neg_m = (m == -INFINITY) ? 0.0f : -m;
+        float2 rs2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+        const float2 c2 = make_float2(c_log2, c_log2), nm2 = make_float2(neg_m, neg_m);
+#pragma unroll
+        for (int c = 0; c < HC / 32; c++) {
+          uint32_t rr[32];
+#pragma unroll
+          for (int e = 0; e < 32; e += 2) {
+            // packed f32x2 multiply and add (separately rounded, as for the max)
+            const float2 a = add2_rn(mul2_rn(make_float2(x[c * 32 + e], x[c * 32 + e + 1]), c2),
+                                     nm2);
+            // half of the pairs on the FMA pipe, half on MUFU
+            const float2 pe = ((e >> 1) & 1) ? ex2_poly2(a) : make_float2(ex2(a.x), ex2(a.y));
+            const uint32_t t0 = __float_as_uint(pe.x) & 0xFFFFE000u;
+            const uint32_t t1 = __float_as_uint(pe.y) & 0xFFFFE000u;
+            rs2[(e >> 1) & 1] = add2_rn(rs2[(e >> 1) & 1],
+                                        make_float2(__uint_as_float(t0), __uint_as_float(t1)));
+            rr[e] = t0;
+            rr[e + 1] = t1;
+          }
+          tmem_st32(t_s(b) + lane_off + g * HC + c * 32, rr);
+        }
+        l += (rs2[0].x + rs2[1].x) + (rs2[0].y + rs2[1].y);
+        tmem_wait_st();
+        tc_fence_before();
+        warp_arrive_leader(bar_p_full(b));
+      }
+      G += t.n_kv;
+      have_prev = true;
+      pt = t;
+      pit = it;
+      pm = m;
+      pl = l;
+      it++;
     }
+    if (have_prev) epilogue();
   }
   // Every MMA of the pair (which reads both CTAs' shared memory and writes both
   // CTAs' TMEM) completes before either CTA frees TMEM or exits.
@@ -1074,12 +1050,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPair, 1)
   tc_fence_before();
   __syncthreads();
   cluster_sync_all();
-#ifdef FA_TRACE
-  if (threadIdx.x == 0 && leader) {
-    atomicAdd(&g_fa_trace[9], (unsigned long long)(clock64() - tr_kstart));
-    atomicAdd(&g_fa_trace[10], 1ull);
-  }
-#endif
   if (warp == 1) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem),
@@ -1122,6 +1092,7 @@ cudaError_t launch_tf32_pair(const FwdParams& p, cudaStream_t s) {
       !make_map(&mv, p.v, D, p.sk, p.bh, BK, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B))
     return cudaErrorInvalidValue;
   static std::atomic<unsigned long long> attr_set{0};  // one bit per device
+  static int sm_count[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   const unsigned long long bit = 1ull << (dev & 63);
@@ -1129,32 +1100,20 @@ cudaError_t launch_tf32_pair(const FwdParams& p, cudaStream_t s) {
     cudaError_t e = cudaFuncSetAttribute(tc_fwd_tf32_pair<D, BK, NKS, NVS>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          C::kSmemBytes);
+    if (e == cudaSuccess)
+      e = cudaDeviceGetAttribute(&sm_count[dev & 63], cudaDevAttrMultiProcessorCount, dev);
     if (e != cudaSuccess) return e;
     attr_set.fetch_or(bit);
   }
   const int n_pairs = (p.sq + 2 * kBM - 1) / (2 * kBM);
-  // grid.y holds the slice index (at most 65535 per launch)
-  for (int b0 = 0; b0 < p.bh; b0 += 65535) {
-    FwdParams q = p;
-    q.bh = min(65535, p.bh - b0);
-    CUtensorMap qk = mk, qv = mv;
-    if (b0 > 0) {
-      q.q += (size_t)b0 * p.sq * D;
-      q.o += (size_t)b0 * p.sq * D;
-      if (q.lse) q.lse += (size_t)b0 * p.sq;
-      q.k += (size_t)b0 * p.sk * D;
-      q.v += (size_t)b0 * p.sk * D;
-      if (!make_map(&qk, q.k, D, p.sk, q.bh, BK / 2, CU_TENSOR_MAP_SWIZZLE_128B) ||
-          !make_map(&qv, q.v, D, p.sk, q.bh, BK, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B))
-        return cudaErrorInvalidValue;
-    }
-    dim3 grid(2, q.bh, n_pairs);
-    tc_fwd_tf32_pair<D, BK, NKS, NVS><<<grid, kThreadsPair, C::kSmemBytes, s>>>(qk, qv, q);
-    count_launch();
-    cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return e;
-  }
-  return cudaSuccess;
+  const long long n_work = (long long)n_pairs * p.bh;
+  // persistent: one cluster (2 SMs) per SM pair, at most one per work tile
+  const int n_clusters = (int)(n_work < sm_count[dev & 63] / 2 ? n_work : sm_count[dev & 63] / 2);
+  if (n_work > INT32_MAX) return cudaErrorInvalidValue;
+  tc_fwd_tf32_pair<D, BK, NKS, NVS><<<dim3(2 * n_clusters), kThreadsPair, C::kSmemBytes, s>>>(
+      mk, mv, p, n_pairs);
+  count_launch();
+  return cudaGetLastError();
 }
 
 }  // namespace
