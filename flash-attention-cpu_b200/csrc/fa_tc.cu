@@ -304,7 +304,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const long long qg = p.q_offset + q0 + r;
     const float c_log2 = p.scale_log2;
     bool ok = !skip;
-    // Stage this row of Q into TMEM, rounded to TF32 (round-to-nearest).
+    // Stage this row of Q into TMEM, multiplied by scale*log2(e) and rounded to
+    // TF32 (round-to-nearest): the scores then come out in log2 units.
     if (ok) {
       const bool valid = r < q_rows;
       const float4* qrow = reinterpret_cast<const float4*>(p.q + ((size_t)bh * p.sq + q0 + r) * D);
@@ -314,10 +315,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int e = 0; e < 8; e++) {
           const float4 v4 = valid ? __ldg(qrow + c * 8 + e) : make_float4(0.f, 0.f, 0.f, 0.f);
-          rr[4 * e + 0] = to_tf32_rna(v4.x);
-          rr[4 * e + 1] = to_tf32_rna(v4.y);
-          rr[4 * e + 2] = to_tf32_rna(v4.z);
-          rr[4 * e + 3] = to_tf32_rna(v4.w);
+          rr[4 * e + 0] = to_tf32_rna(v4.x * c_log2);
+          rr[4 * e + 1] = to_tf32_rna(v4.y * c_log2);
+          rr[4 * e + 2] = to_tf32_rna(v4.z * c_log2);
+          rr[4 * e + 3] = to_tf32_rna(v4.w * c_log2);
         }
         tmem_st32(t_q + lane_off + c * 32, rr);
       }
@@ -366,7 +367,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         mx[t] = fmax3(mx[t], x[e + 4], x[e + 5]);
         mx[t] = fmax3(mx[t], x[e + 6], x[e + 7]);
       }
-      const float m_new = fmaxf(m, __fmul_rn(fmax3(mx[0], mx[1], fmaxf(mx[2], mx[3])), c_log2));
+      const float m_new = fmaxf(m, fmax3(mx[0], mx[1], fmaxf(mx[2], mx[3])));
       float corr = 1.0f;
       bool need = false;
       if (m == -INFINITY) {
@@ -393,24 +394,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         l *= corr;
       }
-      // p = 2^(s*scale*log2e - m), truncated to TF32 exactly as the tensor core
-      // reads it, so the row sum l matches the P the PV MMA multiplies.
-      // The exponent argument is round(x*c) - m with both steps rounded on their
-      // own (no FMA), and m was formed as round(max x * c): the row's maximum
-      // then gives exactly 2^0.  A fused x*c - m would leave the rounding
-      // residual of x*c, which at large scores (|x*c| ~ 1e14, ulp ~ 1e7)
-      // turns 2^residual into 0 or inf.
+      // p = 2^(s - m) (s is already scaled by scale*log2e through Q), truncated
+      // to TF32 exactly as the tensor core reads it, so the row sum l matches
+      // the P the PV MMA multiplies.  m is one of the row's scores, so the
+      // row's maximum gives exactly 2^0 even at huge scores.
       const float neg_m = (m == -INFINITY) ? 0.0f : -m;
       float2 rs2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
-      const float2 c2 = make_float2(c_log2, c_log2), nm2 = make_float2(neg_m, neg_m);
+      const float2 nm2 = make_float2(neg_m, neg_m);
 #pragma unroll
       for (int c = 0; c < BK / 32; c++) {
         uint32_t rr[32];
 #pragma unroll
         for (int e = 0; e < 32; e += 2) {
-          // packed f32x2 multiply and add (separately rounded, as for the max)
-          const float2 a = add2_rn(mul2_rn(make_float2(x[c * 32 + e], x[c * 32 + e + 1]), c2),
-                                   nm2);
+          const float2 a = add2_rn(make_float2(x[c * 32 + e], x[c * 32 + e + 1]), nm2);
           // half of the pairs on the FMA pipe, half on MUFU
           const float2 pe = ((e >> 1) & 1) ? ex2_poly2(a) : make_float2(ex2(a.x), ex2(a.y));
           const uint32_t t0 = __float_as_uint(pe.x) & 0xFFFFE000u;
@@ -907,10 +903,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPair, 1)
 #pragma unroll
           for (int e = 0; e < 8; e++) {
             const float4 v4 = valid ? __ldg(qrow + c * 8 + e) : make_float4(0.f, 0.f, 0.f, 0.f);
-            rr[4 * e + 0] = to_tf32_rna(v4.x);
-            rr[4 * e + 1] = to_tf32_rna(v4.y);
-            rr[4 * e + 2] = to_tf32_rna(v4.z);
-            rr[4 * e + 3] = to_tf32_rna(v4.w);
+            rr[4 * e + 0] = to_tf32_rna(v4.x * c_log2);
+            rr[4 * e + 1] = to_tf32_rna(v4.y * c_log2);
+            rr[4 * e + 2] = to_tf32_rna(v4.z * c_log2);
+            rr[4 * e + 3] = to_tf32_rna(v4.w * c_log2);
           }
           tmem_st32(t_q + lane_off + g * HD + c * 32, rr);
         }
@@ -973,7 +969,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPair, 1)
         const float mx_row = fmaxf(mx_half, slot[(g ^ 1) * 128 + r]);
         // Both halves hold the same m and see the same mx_row, so they take
         // identical rescale decisions.
-        const float m_new = fmaxf(m, __fmul_rn(mx_row, c_log2));
+        const float m_new = fmaxf(m, mx_row);
         float corr = 1.0f;
         bool need = false;
         if (m == -INFINITY) {
@@ -999,22 +995,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPair, 1)
           }
           l *= corr;
         }
-        // The exponent argument is round(x*c) - m with both steps rounded on
-        // their own (no FMA), and m was formed as round(max x * c): the row's
-        // maximum then gives exactly 2^0.  A fused x*c - m would leave the
-        // rounding residual of x*c, which at large scores (|x*c| ~ 1e14, ulp
-        // ~ 1e7) turns 2^residual into 0 or inf.
+        // p = 2^(s - m): s is already scaled by scale*log2e through Q, and m is
+        // one of the row's scores, so the row's maximum gives exactly 2^0.
         const float neg_m = (m == -INFINITY) ? 0.0f : -m;
         float2 rs2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
-        const float2 c2 = make_float2(c_log2, c_log2), nm2 = make_float2(neg_m, neg_m);
+        const float2 nm2 = make_float2(neg_m, neg_m);
 #pragma unroll
         for (int c = 0; c < HC / 32; c++) {
           uint32_t rr[32];
 #pragma unroll
           for (int e = 0; e < 32; e += 2) {
-            // packed f32x2 multiply and add (separately rounded, as for the max)
-            const float2 a = add2_rn(mul2_rn(make_float2(x[c * 32 + e], x[c * 32 + e + 1]), c2),
-                                     nm2);
+            const float2 a = add2_rn(make_float2(x[c * 32 + e], x[c * 32 + e + 1]), nm2);
             // half of the pairs on the FMA pipe, half on MUFU
             const float2 pe = ((e >> 1) & 1) ? ex2_poly2(a) : make_float2(ex2(a.x), ex2(a.y));
             const uint32_t t0 = __float_as_uint(pe.x) & 0xFFFFE000u;
