@@ -593,10 +593,12 @@ struct PairCfg {
   static constexpr int kDHalf = D / 2;                  // head columns of a V tile per CTA
   static constexpr int kKBytes = kKHalf * D * 4;        // per CTA
   static constexpr int kVBytes = BK * kDHalf * 4;       // per CTA
+  static constexpr int kQBytes = kBM * D * 4;          // this CTA's 128 query rows
   static constexpr int kOffK = 0;
   static constexpr int kOffV = NKS * kKBytes;
-  static constexpr int kOffBar = kOffV + NVS * kVBytes;
-  static constexpr int kNumBars = 1 + 2 * NKS + 2 * NVS + 2 + 2 + 3;
+  static constexpr int kOffQ = kOffV + NVS * kVBytes;   // D/32 swizzled [128 x 32] chunks
+  static constexpr int kOffBar = kOffQ + kQBytes;
+  static constexpr int kNumBars = 1 + 2 * NKS + 2 * NVS + 2 + 2 + 3 + 2;
   static constexpr int kOffRed = (kOffBar + kNumBars * 8 + 16 + 15) / 16 * 16;
   static constexpr int kSmemBytes = kOffRed + 4 * 2 * 128 * 4 + 1024;
   static constexpr int kTmemColsUsed = 2 * D + 2 * BK;
@@ -612,7 +614,9 @@ constexpr int kThreadsPair = 384;  // 12 warps: 2 producers, MMA, idle, 2 softma
 template <int D, int BK, int NKS, int NVS>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPair, 1)
     tc_fwd_tf32_pair(const __grid_constant__ CUtensorMap tmK,
-                     const __grid_constant__ CUtensorMap tmV, FwdParams p, int n_pairs) {
+                     const __grid_constant__ CUtensorMap tmV,
+                     const __grid_constant__ CUtensorMap tmQ,
+                     const __grid_constant__ CUtensorMap tmO, FwdParams p, int n_pairs) {
   // Persistent: cluster c computes work tiles w = c, c + C, ... (C clusters),
   // each tile = 256 query rows (a pair) of one slice, heaviest causal tiles
   // first.  Every ring and buffer index continues across tiles through the
@@ -648,6 +652,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPair, 1)
   // which its softmax produces only after the previous tile's O was read out,
   // so no separate "O free" barrier is needed.
   const uint32_t bar_o_final = bar0 + 8u * (kB2 + 6);
+  // Q staging buffer (this CTA's): q_smem_full completes when a tile's Q rows
+  // have landed (TMA, issued by the K producer); q_smem_free when the softmax
+  // warps have copied them into TMEM and the previous tile's O, written over
+  // them, has been stored out, so the next tile's rows may be loaded.
+  const uint32_t bar_q_smem_full = bar0 + 8u * (kB2 + 7);
+  const uint32_t bar_q_smem_free = bar0 + 8u * (kB2 + 8);
+  const uint32_t sQ = sbase + C::kOffQ;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kOffBar + C::kNumBars * 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   auto at_leader = [&](uint32_t bar) { return map_to_rank(bar, 0); };
@@ -694,6 +705,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPair, 1)
     mbar_init(bar_o_done, 1);
     mbar_init(bar_drain, 1);
     mbar_init(bar_o_final, 1);
+    mbar_init(bar_q_smem_full, 1);
+    mbar_init(bar_q_smem_free, 1);  // one softmax thread, after every warp is done with it
     *abort_flag = (*(volatile int*)p.err != 0) ? 1 : 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -718,12 +731,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPair, 1)
     const bool is_k = warp == 0;
     const int NS = is_k ? NKS : NVS;
     if (lane == 0 && !skip) {
-      int G = 0;  // global key-block counter
+      int G = 0;   // global key-block counter
+      int qit = 0;  // tiles whose Q rows were loaded (K producer)
       bool ok = true;
       for (int k = 0; k * n_clusters < n_work && ok; k++) {
         const int w = work_of(k);
         if (w >= n_work) continue;
         const Tile t = tile_of(w);
+        if (is_k) {
+          // This CTA's 128 rows of the tile's Q, as D/32 swizzled [128 x 32]
+          // chunks (rows past the slice read as zeros), once the previous
+          // tile's rows have been copied into TMEM.
+          if (qit > 0) ok = mbar_wait(bar_q_smem_free, (qit - 1) & 1, abort_flag, p.err);
+          if (!ok) break;
+          mbar_expect_tx(bar_q_smem_full, C::kQBytes);
+          for (int c = 0; c < D / 32; c++)
+            tma_load_3d(sQ + c * (kBM * 128), &tmQ, bar_q_smem_full, 32 * c, t.q0, t.bh);
+          qit++;
+        }
         for (int j = 0; j < t.n_kv && ok; j++, G++) {
           const int s = G % NS;
           if (G >= NS)
@@ -752,6 +777,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPair, 1)
         for (int g = max(0, G - NS); g < G; g++)
           mbar_wait(is_k ? bar_k_full(g % NS) : bar_v_full(g % NS), (g / NS) & 1, &no_abort,
                     p.err);
+      if (is_k && qit > 0) mbar_wait(bar_q_smem_full, (qit - 1) & 1, &no_abort, p.err);
     }
     __syncwarp();
   } else if (warp == 1) {
@@ -843,66 +869,80 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPair, 1)
     Tile pt{};
     int pit = 0;
     float pm = -INFINITY, pl = 0.0f;
-    auto epilogue = [&]() {
-      // all 8 softmax warps of the quarter pair reach this on every path
-      bool w = ok;
+    // The previous tile's O (scaled by 1/l) into the Q buffer, in the same
+    // swizzled layout, for a TMA store: returns false on a failure.  The Q rows
+    // this thread wrote over were its own, already copied into TMEM.
+    auto epilogue_smem = [&](bool go, float* l_out) -> bool {
+      // both warps of the quarter pair reach this on every path
+      bool w = go;
       if (w) w = __all_sync(0xffffffffu, mbar_wait(bar_o_final, pit & 1, abort_flag, p.err));
       if (*abort_flag) w = false;
       // row-sum exchange slot alternates by tile, so a slot is rewritten only
       // after both warps have passed the next epilogue's barrier
       float* lslot = red + 512 + (pit & 1) * 256;
       lslot[g * 128 + r] = pl;
-      ok = !bar_any(1 + quarter, 64, !w);
+      const bool fail = bar_any(1 + quarter, 64, !w);
       const float l_row = pl + lslot[(g ^ 1) * 128 + r];
-      if (ok) {
-        tc_fence_after();
-        const float inv_l = l_row > 0.0f ? 1.0f / l_row : 0.0f;
-        const bool row_ok = r < pt.q_rows;
-        float* orow = p.o + ((size_t)pt.bh * p.sq + pt.q0 + r) * D + g * HD;
+      *l_out = l_row;
+      if (fail) return false;
+      tc_fence_after();
+      const float inv_l = l_row > 0.0f ? 1.0f / l_row : 0.0f;
 #pragma unroll
-        for (int c = 0; c < HD / 32; c++) {
-          uint32_t rr[32];
-          if (pt.n_kv > 0) {
-            tmem_ld32(t_o + lane_off + g * HD + c * 32, rr);
-            tmem_wait_ld_regs(rr);
-          } else {
+      for (int c = 0; c < HD / 32; c++) {
+        uint32_t rr[32];
+        if (pt.n_kv > 0) {
+          tmem_ld32(t_o + lane_off + g * HD + c * 32, rr);
+          tmem_wait_ld_regs(rr);
+        } else {
 #pragma unroll
-            for (int e = 0; e < 32; e++) rr[e] = 0u;
-          }
-          if (row_ok) {
-#pragma unroll
-            for (int e = 0; e < 32; e += 4) {
-              float4 v4 =
-                  make_float4(__uint_as_float(rr[e]) * inv_l, __uint_as_float(rr[e + 1]) * inv_l,
-                              __uint_as_float(rr[e + 2]) * inv_l, __uint_as_float(rr[e + 3]) * inv_l);
-              *reinterpret_cast<float4*>(orow + c * 32 + e) = v4;
-            }
-          }
+          for (int e = 0; e < 32; e++) rr[e] = 0u;
         }
-        if (row_ok && g == 0 && p.lse)
-          p.lse[(size_t)pt.bh * p.sq + pt.q0 + r] =
-              l_row > 0.0f ? (pm + __log2f(l_row)) * 0.69314718055994530942f : -INFINITY;
-        tc_fence_before();  // O reads done before this thread's next barrier arrive
+        uint8_t* orow = smem + C::kOffQ + (g * (HD / 32) + c) * (kBM * 128) + r * 128;
+#pragma unroll
+        for (int e = 0; e < 8; e++)
+          *reinterpret_cast<float4*>(orow + ((e ^ (r & 7)) << 4)) = make_float4(
+              __uint_as_float(rr[4 * e]) * inv_l, __uint_as_float(rr[4 * e + 1]) * inv_l,
+              __uint_as_float(rr[4 * e + 2]) * inv_l, __uint_as_float(rr[4 * e + 3]) * inv_l);
       }
+      tc_fence_before();  // O reads done before this thread's next barrier arrive
+      return true;
+    };
+    // After every softmax warp passed the 256-thread barrier that follows
+    // epilogue_smem: one thread stores the tile (rows past the slice are
+    // clipped by the tensor map), waits until the store has read the buffer,
+    // and frees the buffer for the next Q.
+    auto store_out = [&](bool last) {
+      if (pt.q_rows > 0)
+        for (int c = 0; c < D / 32; c++)
+          tma_store_3d(&tmO, sQ + c * (kBM * 128), 32 * c, pt.q0, pt.bh);
+      bulk_commit();
+      if (last)
+        bulk_wait_all();
+      else
+        bulk_wait_read_all();
     };
     int G = 0, it = 0;
-    for (int k = 0; k * n_clusters < n_work && ok; k++) {
+    // Every softmax warp runs every tile iteration (a failure only skips the
+    // work), so that all eight reach the 256-thread barrier equally often.
+    for (int k = 0; k * n_clusters < n_work; k++) {
       const int w = work_of(k);
       if (w >= n_work) continue;
       const Tile t = tile_of(w);
       const long long qg = p.q_offset + t.q0 + r;
-      {
-        // Stage this tile's Q.  The previous tile's QK^T MMAs are complete: its
-        // last S was visible before its last P was written.
-        const bool valid = r < t.q_rows;
-        const float4* qrow = reinterpret_cast<const float4*>(
-            p.q + ((size_t)t.bh * p.sq + t.q0 + r) * D + g * HD);
+      // Stage this tile's Q from the shared-memory buffer (128B-swizzled rows:
+      // 16-byte unit u of row r sits at unit u ^ (r & 7), so 32 threads reading
+      // one unit of 32 rows hit every bank).  The previous tile's QK^T MMAs are
+      // complete: its last S was visible before its last P was written.
+      const bool okq =
+          ok && __all_sync(0xffffffffu, mbar_wait(bar_q_smem_full, it & 1, abort_flag, p.err));
+      if (okq) {
 #pragma unroll
         for (int c = 0; c < HD / 32; c++) {
+          const uint8_t* qrow = smem + C::kOffQ + (g * (HD / 32) + c) * (kBM * 128) + r * 128;
           uint32_t rr[32];
 #pragma unroll
           for (int e = 0; e < 8; e++) {
-            const float4 v4 = valid ? __ldg(qrow + c * 8 + e) : make_float4(0.f, 0.f, 0.f, 0.f);
+            const float4 v4 = *reinterpret_cast<const float4*>(qrow + ((e ^ (r & 7)) << 4));
             rr[4 * e + 0] = to_tf32_rna(v4.x * c_log2);
             rr[4 * e + 1] = to_tf32_rna(v4.y * c_log2);
             rr[4 * e + 2] = to_tf32_rna(v4.z * c_log2);
@@ -914,10 +954,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPair, 1)
         tc_fence_before();
         warp_arrive_leader(bar_q_full);
       }
-      if (have_prev) {
-        epilogue();
-        if (!ok) break;
+      float l_prev = 0.0f;
+      const bool oke = have_prev ? epilogue_smem(okq, &l_prev) : okq;
+      fence_proxy_async_smem();
+      if (bar_any(5, 256, !oke)) ok = false;
+      if (ok && warp == kSoftmaxWarp0 && lane == 0) {
+        if (have_prev) store_out(false);
+        mbar_arrive(bar_q_smem_free);
       }
+      if (ok && have_prev && g == 0 && r < pt.q_rows && p.lse)
+        p.lse[(size_t)pt.bh * p.sq + pt.q0 + r] =
+            l_prev > 0.0f ? (pm + __log2f(l_prev)) * 0.69314718055994530942f : -INFINITY;
       float m = -INFINITY, l = 0.0f;  // l: this half's partial row sum
       for (int j = 0; j < t.n_kv && ok; j++) {
         const int Gj = G + j, b = Gj & 1;
@@ -1030,7 +1077,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPair, 1)
       pl = l;
       it++;
     }
-    if (have_prev) epilogue();
+    if (have_prev) {
+      float l_prev = 0.0f;
+      const bool oke = epilogue_smem(ok, &l_prev);
+      fence_proxy_async_smem();
+      if (!bar_any(5, 256, !oke)) {
+        if (warp == kSoftmaxWarp0 && lane == 0) store_out(true);
+        if (g == 0 && r < pt.q_rows && p.lse)
+          p.lse[(size_t)pt.bh * p.sq + pt.q0 + r] =
+              l_prev > 0.0f ? (pm + __log2f(l_prev)) * 0.69314718055994530942f : -INFINITY;
+      }
+    }
   }
   // Every MMA of the pair (which reads both CTAs' shared memory and writes both
   // CTAs' TMEM) completes before either CTA frees TMEM or exits.
@@ -1079,8 +1136,11 @@ template <int D, int BK, int NKS, int NVS>
 cudaError_t launch_tf32_pair(const FwdParams& p, cudaStream_t s) {
   using C = PairCfg<D, BK, NKS, NVS>;
   CUtensorMap mk, mv;
+  CUtensorMap mq, mo;
   if (!make_map(&mk, p.k, D, p.sk, p.bh, BK / 2, CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !make_map(&mv, p.v, D, p.sk, p.bh, BK, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B))
+      !make_map(&mv, p.v, D, p.sk, p.bh, BK, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B) ||
+      !make_map(&mq, p.q, D, p.sq, p.bh, kBM, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !make_map(&mo, p.o, D, p.sq, p.bh, kBM, CU_TENSOR_MAP_SWIZZLE_128B))
     return cudaErrorInvalidValue;
   static std::atomic<unsigned long long> attr_set{0};  // one bit per device
   static int sm_count[64] = {};
@@ -1102,7 +1162,7 @@ cudaError_t launch_tf32_pair(const FwdParams& p, cudaStream_t s) {
   const int n_clusters = (int)(n_work < sm_count[dev & 63] / 2 ? n_work : sm_count[dev & 63] / 2);
   if (n_work > INT32_MAX) return cudaErrorInvalidValue;
   tc_fwd_tf32_pair<D, BK, NKS, NVS><<<dim3(2 * n_clusters), kThreadsPair, C::kSmemBytes, s>>>(
-      mk, mv, p, n_pairs);
+      mk, mv, mq, mo, p, n_pairs);
   count_launch();
   return cudaGetLastError();
 }
@@ -1139,7 +1199,7 @@ cudaError_t launch_tc(const FwdParams& p, int precision, float*, size_t, cudaStr
   const bool single = p.sq <= kBM;
   if (p.d == 128)
     return single ? launch_tf32<128, 128, FA_D128_VK, 2, FA_D128_NVS>(p, s)
-                  : launch_tf32_pair<128, 128, 3, 3>(p, s);
+                  : launch_tf32_pair<128, 128, 2, 2>(p, s);
   if (p.d == 64)
     return single ? launch_tf32<64, 128, 128, 3, 3>(p, s) : launch_tf32_pair<64, 128, 3, 3>(p, s);
   return cudaErrorInvalidValue;
