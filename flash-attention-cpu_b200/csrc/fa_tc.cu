@@ -72,10 +72,11 @@ __device__ unsigned long long g_fa_trace[32];
 #define FA_TR_ADD(slot) atomicAdd(&g_fa_trace[slot], (unsigned long long)(clock64() - tr_t0))
 #define FA_TR_CNT(slot) atomicAdd(&g_fa_trace[slot], 1ull)
 // per-tile event timestamps of one CTA pair (blockIdx.y == 0, blockIdx.z == 0)
-__device__ long long g_fa_events[12][256];
+// (CTAs 0 and 1 of the first cluster: [cta][kind][block]; clock64 of each SM)
+__device__ long long g_fa_events[2][24][256];
 #define FA_EV(kind, j)                                                              \
-  if (blockIdx.y == 0 && blockIdx.z == 0 && blockIdx.x == 0 && (j) < 256)           \
-  g_fa_events[kind][j] = clock64()
+  if (blockIdx.y == 0 && blockIdx.z == 0 && blockIdx.x < 2 && (j) < 256)            \
+  g_fa_events[blockIdx.x][kind][j] = clock64()
 #else
 #define FA_EV(kind, j) \
   do {                 \
@@ -598,7 +599,7 @@ struct PairCfg {
   static constexpr int kOffV = NKS * kKBytes;
   static constexpr int kOffQ = kOffV + NVS * kVBytes;   // D/32 swizzled [128 x 32] chunks
   static constexpr int kOffBar = kOffQ + kQBytes;
-  static constexpr int kNumBars = 1 + 2 * NKS + 2 * NVS + 2 + 2 + 3 + 2;
+  static constexpr int kNumBars = 1 + 2 * NKS + 2 * NVS + 2 + 2 + 3 + 3;
   static constexpr int kOffRed = (kOffBar + kNumBars * 8 + 16 + 15) / 16 * 16;
   static constexpr int kSmemBytes = kOffRed + 4 * 2 * 128 * 4 + 1024;
   static constexpr int kTmemColsUsed = 2 * D + 2 * BK;
@@ -653,11 +654,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPair, 1)
   // so no separate "O free" barrier is needed.
   const uint32_t bar_o_final = bar0 + 8u * (kB2 + 6);
   // Q staging buffer (this CTA's): q_smem_full completes when a tile's Q rows
-  // have landed (TMA, issued by the K producer); q_smem_free when the softmax
-  // warps have copied them into TMEM and the previous tile's O, written over
-  // them, has been stored out, so the next tile's rows may be loaded.
+  // have landed (TMA, issued by the K producer); q_smem_free when they were
+  // copied into TMEM and the previous tile's O, written over them, has been
+  // stored out (warp 3), so the next tile's rows may be loaded.
   const uint32_t bar_q_smem_full = bar0 + 8u * (kB2 + 7);
   const uint32_t bar_q_smem_free = bar0 + 8u * (kB2 + 8);
+  // o_smem_full: the softmax warps are done with the buffer for one tile step
+  // (this tile's Q copied into TMEM and the previous tile's O written over
+  // it); warp 3 then stores that O out and frees the buffer.
+  const uint32_t bar_o_smem_full = bar0 + 8u * (kB2 + 9);
   const uint32_t sQ = sbase + C::kOffQ;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kOffBar + C::kNumBars * 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -706,7 +711,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPair, 1)
     mbar_init(bar_drain, 1);
     mbar_init(bar_o_final, 1);
     mbar_init(bar_q_smem_full, 1);
-    mbar_init(bar_q_smem_free, 1);  // one softmax thread, after every warp is done with it
+    mbar_init(bar_q_smem_free, 1);  // warp 3
+    mbar_init(bar_o_smem_full, 8);  // 8 softmax warps of this CTA
     *abort_flag = (*(volatile int*)p.err != 0) ? 1 : 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -744,6 +750,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPair, 1)
           // tile's rows have been copied into TMEM.
           if (qit > 0) ok = mbar_wait(bar_q_smem_free, (qit - 1) & 1, abort_flag, p.err);
           if (!ok) break;
+          FA_EV(19, G);
           mbar_expect_tx(bar_q_smem_full, C::kQBytes);
           for (int c = 0; c < D / 32; c++)
             tma_load_3d(sQ + c * (kBM * 128), &tmQ, bar_q_smem_full, 32 * c, t.q0, t.bh);
@@ -755,6 +762,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPair, 1)
             ok = mbar_wait(is_k ? bar_k_empty(s) : bar_v_empty(s), ((G / NS) & 1) ^ 1, abort_flag,
                            p.err);
           if (!ok) break;
+          FA_EV(is_k ? 12 : 11, G);
           const uint32_t full = at_leader(is_k ? bar_k_full(s) : bar_v_full(s));
           if (is_k) {
             mbar_expect_tx_cluster(full, C::kKBytes);
@@ -795,8 +803,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPair, 1)
         const int b = G & 1, sv = G % NVS;
         if (!__all_sync(0xffffffffu, mbar_wait(bar_p_full(b), (G >> 1) & 1, abort_flag, p.err)))
           return false;
+        if (lane == 0) FA_EV(2, G);
         if (!__all_sync(0xffffffffu, mbar_wait(bar_v_full(sv), (G / NVS) & 1, abort_flag, p.err)))
           return false;
+        if (lane == 0) FA_EV(3, G);
         tc_fence_after();
         // 8 keys per MMA = two 4-row groups (SBO = 512 B); 32-column chunks LBO apart
         const uint64_t vdesc = smem_desc(sV + sv * C::kVBytes, BK * 128, 512, kLayoutSw128Base32);
@@ -806,6 +816,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPair, 1)
                             (j > 0 || kk > 0) ? 1u : 0u);
         commit_both(bar_v_empty(sv));
         commit_both(bar_o_done);
+        if (lane == 0) FA_EV(4, G);
         return true;
       };
       bool ok = true;
@@ -819,8 +830,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPair, 1)
         tc_fence_after();
         for (int j = 0; j < t.n_kv && ok; j++) {
           const int Gj = G + j, s = Gj % NKS, b = Gj & 1;
+          if (lane == 0) FA_EV(13, Gj);
           ok = __all_sync(0xffffffffu, mbar_wait(bar_k_full(s), (Gj / NKS) & 1, abort_flag, p.err));
           if (!ok) break;
+          if (lane == 0) FA_EV(0, Gj);
           tc_fence_after();
           const uint64_t kdesc = smem_desc(sK + s * C::kKBytes, 16, 1024, kLayoutSw128);
 #pragma unroll
@@ -830,6 +843,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPair, 1)
                               idesc_qk, kk > 0 ? 1u : 0u);
           commit_both(bar_s_full(b));
           commit_both(bar_k_empty(s));
+          if (lane == 0) FA_EV(1, Gj);
           if (j > 0) ok = issue_pv(Gj - 1, j - 1);
         }
         if (ok && t.n_kv > 0) ok = issue_pv(G + t.n_kv - 1, t.n_kv - 1);
@@ -839,6 +853,41 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPair, 1)
         it++;
       }
       commit_both(bar_drain);
+    }
+    __syncwarp();
+  } else if (warp == 3) {
+    // ------------------------------ O store (one lane): after the softmax warps
+    // are done with the buffer for a tile step, TMA-store the previous tile's O
+    // from it (rows past the slice are clipped by the tensor map), wait until
+    // the store has read it, and free it for the next tile's Q.
+    if (lane == 0 && !skip) {
+      bool ok = true, have_prev = false;
+      int it = 0;
+      Tile pt{};
+      auto store = [&](bool last) {
+        if (pt.q_rows > 0)
+          for (int c = 0; c < D / 32; c++)
+            tma_store_3d(&tmO, sQ + c * (kBM * 128), 32 * c, pt.q0, pt.bh);
+        bulk_commit();
+        if (last)
+          bulk_wait_all();
+        else
+          bulk_wait_read_all();
+      };
+      for (int k = 0; k * n_clusters < n_work && ok; k++) {
+        const int w = work_of(k);
+        if (w >= n_work) continue;
+        const Tile t = tile_of(w);
+        ok = mbar_wait(bar_o_smem_full, it & 1, abort_flag, p.err);
+        if (!ok) break;
+        if (have_prev) store(false);
+        FA_EV(18, it);
+        mbar_arrive(bar_q_smem_free);
+        have_prev = true;
+        pt = t;
+        it++;
+      }
+      if (ok && have_prev && mbar_wait(bar_o_smem_full, it & 1, abort_flag, p.err)) store(true);
     }
     __syncwarp();
   } else if (warp >= kSoftmaxWarp0) {
@@ -907,23 +956,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPair, 1)
       tc_fence_before();  // O reads done before this thread's next barrier arrive
       return true;
     };
-    // After every softmax warp passed the 256-thread barrier that follows
-    // epilogue_smem: one thread stores the tile (rows past the slice are
-    // clipped by the tensor map), waits until the store has read the buffer,
-    // and frees the buffer for the next Q.
-    auto store_out = [&](bool last) {
-      if (pt.q_rows > 0)
-        for (int c = 0; c < D / 32; c++)
-          tma_store_3d(&tmO, sQ + c * (kBM * 128), 32 * c, pt.q0, pt.bh);
-      bulk_commit();
-      if (last)
-        bulk_wait_all();
-      else
-        bulk_wait_read_all();
-    };
     int G = 0, it = 0;
-    // Every softmax warp runs every tile iteration (a failure only skips the
-    // work), so that all eight reach the 256-thread barrier equally often.
+    // (a failure only skips the remaining work; both warps of a quarter pair
+    // still meet at their per-block and epilogue barriers)
     for (int k = 0; k * n_clusters < n_work; k++) {
       const int w = work_of(k);
       if (w >= n_work) continue;
@@ -935,6 +970,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPair, 1)
       // complete: its last S was visible before its last P was written.
       const bool okq =
           ok && __all_sync(0xffffffffu, mbar_wait(bar_q_smem_full, it & 1, abort_flag, p.err));
+      if (lane == 0 && quarter == 0 && g == 0) FA_EV(14, G);
       if (okq) {
 #pragma unroll
         for (int c = 0; c < HD / 32; c++) {
@@ -954,13 +990,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPair, 1)
         tc_fence_before();
         warp_arrive_leader(bar_q_full);
       }
+      if (lane == 0 && quarter == 0 && g == 0) FA_EV(15, G);
       float l_prev = 0.0f;
       const bool oke = have_prev ? epilogue_smem(okq, &l_prev) : okq;
-      fence_proxy_async_smem();
-      if (bar_any(5, 256, !oke)) ok = false;
-      if (ok && warp == kSoftmaxWarp0 && lane == 0) {
-        if (have_prev) store_out(false);
-        mbar_arrive(bar_q_smem_free);
+      if (lane == 0 && quarter == 0 && g == 0) FA_EV(16, G);
+      if (!oke) ok = false;
+      if (ok) {
+        // this warp's O rows (if any) reach the TMA store through warp 3
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar_o_smem_full);
       }
       if (ok && have_prev && g == 0 && r < pt.q_rows && p.lse)
         p.lse[(size_t)pt.bh * p.sq + pt.q0 + r] =
@@ -970,6 +1009,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPair, 1)
         const int Gj = G + j, b = Gj & 1;
         const bool wt =
             __all_sync(0xffffffffu, mbar_wait(bar_s_full(b), (Gj >> 1) & 1, abort_flag, p.err));
+        if (lane == 0 && quarter == 0) FA_EV(5 + 3 * g, Gj);
         tc_fence_after();
         float x[HC];
         if (wt) {
@@ -1013,6 +1053,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPair, 1)
           ok = false;
           break;
         }
+        if (lane == 0 && quarter == 0) FA_EV(6 + 3 * g, Gj);
         const float mx_row = fmaxf(mx_half, slot[(g ^ 1) * 128 + r]);
         // Both halves hold the same m and see the same mx_row, so they take
         // identical rescale decisions.
@@ -1068,6 +1109,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPair, 1)
         tmem_wait_st();
         tc_fence_before();
         warp_arrive_leader(bar_p_full(b));
+        if (lane == 0 && quarter == 0) FA_EV(7 + 3 * g, Gj);
       }
       G += t.n_kv;
       have_prev = true;
@@ -1079,10 +1121,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPair, 1)
     }
     if (have_prev) {
       float l_prev = 0.0f;
-      const bool oke = epilogue_smem(ok, &l_prev);
-      fence_proxy_async_smem();
-      if (!bar_any(5, 256, !oke)) {
-        if (warp == kSoftmaxWarp0 && lane == 0) store_out(true);
+      if (epilogue_smem(ok, &l_prev)) {
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar_o_smem_full);
         if (g == 0 && r < pt.q_rows && p.lse)
           p.lse[(size_t)pt.bh * p.sq + pt.q0 + r] =
               l_prev > 0.0f ? (pm + __log2f(l_prev)) * 0.69314718055994530942f : -INFINITY;
