@@ -400,26 +400,26 @@ __global__ void __launch_bounds__(kThreads, 1)
       // the P the PV MMA multiplies.  m is one of the row's scores, so the
       // row's maximum gives exactly 2^0 even at huge scores.
       const float neg_m = (m == -INFINITY) ? 0.0f : -m;
-      float2 rs2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
-      const float2 nm2 = make_float2(neg_m, neg_m);
+      // one add, one MUFU exponential, one mask and one add per score
+      float rs[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int c = 0; c < BK / 32; c++) {
         uint32_t rr[32];
 #pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          const float2 a = add2_rn(make_float2(x[c * 32 + e], x[c * 32 + e + 1]), nm2);
-          // half of the pairs on the FMA pipe, half on MUFU
-          const float2 pe = ((e >> 1) & 1) ? ex2_poly2(a) : make_float2(ex2(a.x), ex2(a.y));
-          const uint32_t t0 = __float_as_uint(pe.x) & 0xFFFFE000u;
-          const uint32_t t1 = __float_as_uint(pe.y) & 0xFFFFE000u;
-          rs2[(e >> 1) & 1] = add2_rn(rs2[(e >> 1) & 1],
-                                      make_float2(__uint_as_float(t0), __uint_as_float(t1)));
-          rr[e] = t0;
-          rr[e + 1] = t1;
+        for (int e = 0; e < 32; e += 8) {
+          float pe[8];
+#pragma unroll
+          for (int u = 0; u < 8; u++) pe[u] = ex2(__fadd_rn(x[c * 32 + e + u], neg_m));
+#pragma unroll
+          for (int u = 0; u < 8; u++) {
+            const uint32_t tb = __float_as_uint(pe[u]) & 0xFFFFE000u;
+            rs[u & 3] += __uint_as_float(tb);
+            rr[e + u] = tb;
+          }
         }
         tmem_st32(t_s(b) + lane_off + c * 32, rr);
       }
-      l += (rs2[0].x + rs2[1].x) + (rs2[0].y + rs2[1].y);
+      l += (rs[0] + rs[1]) + (rs[2] + rs[3]);
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(bar_p_full(b));
@@ -588,7 +588,7 @@ __device__ __forceinline__ bool bar_any(uint32_t id, uint32_t n, bool v) {
   return r != 0;
 }
 
-template <int D, int BK, int NKS, int NVS>
+template <int D, int BK, int NKS, int NVS, int NG>
 struct PairCfg {
   static constexpr int kKHalf = BK / 2;                 // keys of a K tile held per CTA
   static constexpr int kDHalf = D / 2;                  // head columns of a V tile per CTA
@@ -601,7 +601,8 @@ struct PairCfg {
   static constexpr int kOffBar = kOffQ + kQBytes;
   static constexpr int kNumBars = 1 + 2 * NKS + 2 * NVS + 2 + 2 + 3 + 3;
   static constexpr int kOffRed = (kOffBar + kNumBars * 8 + 16 + 15) / 16 * 16;
-  static constexpr int kSmemBytes = kOffRed + 4 * 2 * 128 * 4 + 1024;
+  // softmax exchange: row maxima [2 blocks][NG][128], row sums [2 tiles][NG][128]
+  static constexpr int kSmemBytes = kOffRed + 4 * NG * 128 * 4 + 1024;
   static constexpr int kTmemColsUsed = 2 * D + 2 * BK;
   static constexpr int kTmemCols = kTmemColsUsed <= 256 ? 256 : 512;
   static_assert(D % 64 == 0 && D <= 128, "pair kernel: D in {64, 128}");
@@ -610,10 +611,11 @@ struct PairCfg {
   static_assert(kSmemBytes <= 232448, "shared-memory budget");
 };
 
-constexpr int kThreadsPair = 384;  // 12 warps: 2 producers, MMA, idle, 2 softmax warpgroups
+// 4 + 4*NG warps: K producer, MMA, V producer, O store, then NG softmax warpgroups.
+constexpr int pair_threads(int ng) { return 128 + 128 * ng; }
 
-template <int D, int BK, int NKS, int NVS>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPair, 1)
+template <int D, int BK, int NKS, int NVS, int NG>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(NG), 1)
     tc_fwd_tf32_pair(const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV,
                      const __grid_constant__ CUtensorMap tmQ,
@@ -625,7 +627,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPair, 1)
   // while the current one finishes; the softmax warps stage the next tile's Q
   // before writing out the current tile's O, so QK^T of the next tile overlaps
   // that epilogue.
-  using C = PairCfg<D, BK, NKS, NVS>;
+  using C = PairCfg<D, BK, NKS, NVS, NG>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -694,7 +696,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPair, 1)
   };
 
   if (threadIdx.x == 0) {
-    mbar_init(bar_q_full, 16);  // 8 softmax warps x 2 CTAs
+    mbar_init(bar_q_full, 8 * NG);  // 4*NG softmax warps x 2 CTAs
     for (int s = 0; s < NKS; s++) {
       mbar_init(bar_k_full(s), 2);
       mbar_init(bar_k_empty(s), 1);
@@ -705,14 +707,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPair, 1)
     }
     for (int b = 0; b < 2; b++) {
       mbar_init(bar_s_full(b), 1);
-      mbar_init(bar_p_full(b), 16);
+      mbar_init(bar_p_full(b), 8 * NG);
     }
     mbar_init(bar_o_done, 1);
     mbar_init(bar_drain, 1);
     mbar_init(bar_o_final, 1);
     mbar_init(bar_q_smem_full, 1);
     mbar_init(bar_q_smem_free, 1);  // warp 3
-    mbar_init(bar_o_smem_full, 8);  // 8 softmax warps of this CTA
+    mbar_init(bar_o_smem_full, 4 * NG);  // the softmax warps of this CTA
     *abort_flag = (*(volatile int*)p.err != 0) ? 1 : 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -891,18 +893,28 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPair, 1)
     }
     __syncwarp();
   } else if (warp >= kSoftmaxWarp0) {
-    // ------------------------------ softmax: two warpgroups, thread = (row, half)
-    // Warpgroup g (warps 4-7: g = 0, warps 8-11: g = 1) handles columns
-    // [g*BK/2, (g+1)*BK/2) of every score row and O columns [g*D/2, (g+1)*D/2);
-    // the two halves of a row exchange partial maxima once per block through
-    // shared memory and keep separate partial row sums until the epilogue.
-    constexpr int HC = BK / 2, HD = D / 2;
+    // ------------------------------ softmax: NG warpgroups, thread = (row, part)
+    // Warpgroup g (warps 4+4g .. 7+4g) handles columns [g*BK/NG, (g+1)*BK/NG)
+    // of every score row and O columns [g*D/NG, (g+1)*D/NG); the NG parts of a
+    // row exchange partial maxima once per block through shared memory and
+    // keep separate partial row sums until the epilogue.  The NG warps holding
+    // the same 32 rows (warps 4+q, 8+q, ...) run on the same scheduler.
+    constexpr int HC = BK / NG, HD = D / NG;
+    constexpr int CW = HD >= 32 ? 32 : 16;  // O / Q columns per TMEM access
+    static_assert(HC % 32 == 0 && HD % CW == 0, "softmax column split");
     const int g = (warp - kSoftmaxWarp0) >> 2;
     const int quarter = warp & 3;  // TMEM lanes 32*quarter..
     const int r = quarter * 32 + lane;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const float c_log2 = p.scale_log2;
-    float* red = reinterpret_cast<float*>(smem + C::kOffRed);  // [4][2][128]
+    float* red = reinterpret_cast<float*>(smem + C::kOffRed);
+    // the byte address of columns [col, col+CW) of row r in the swizzled
+    // [128 x 32] chunks of the Q / O buffer: 16-byte unit u of row r sits at
+    // unit u ^ (r & 7), so 32 threads touching one unit of 32 rows hit every bank
+    auto buf_row = [&](int col) {
+      return smem + C::kOffQ + (col >> 5) * (kBM * 128) + r * 128;
+    };
+    auto buf_unit = [&](int col, int e) { return ((((col & 31) >> 2) + e) ^ (r & 7)) << 4; };
     auto warp_arrive_leader = [&](uint32_t bar) {
       __syncwarp();
       if (lane == 0) {
@@ -922,34 +934,37 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPair, 1)
     // swizzled layout, for a TMA store: returns false on a failure.  The Q rows
     // this thread wrote over were its own, already copied into TMEM.
     auto epilogue_smem = [&](bool go, float* l_out) -> bool {
-      // both warps of the quarter pair reach this on every path
+      // all NG warps of the quarter reach this on every path
       bool w = go;
       if (w) w = __all_sync(0xffffffffu, mbar_wait(bar_o_final, pit & 1, abort_flag, p.err));
       if (*abort_flag) w = false;
       // row-sum exchange slot alternates by tile, so a slot is rewritten only
-      // after both warps have passed the next epilogue's barrier
-      float* lslot = red + 512 + (pit & 1) * 256;
+      // after every warp of the quarter has passed the next epilogue's barrier
+      float* lslot = red + 2 * NG * 128 + (pit & 1) * (NG * 128);
       lslot[g * 128 + r] = pl;
-      const bool fail = bar_any(1 + quarter, 64, !w);
-      const float l_row = pl + lslot[(g ^ 1) * 128 + r];
+      const bool fail = bar_any(1 + quarter, 32 * NG, !w);
+      float l_row = 0.0f;
+#pragma unroll
+      for (int i = 0; i < NG; i++) l_row += lslot[i * 128 + r];
       *l_out = l_row;
       if (fail) return false;
       tc_fence_after();
       const float inv_l = l_row > 0.0f ? 1.0f / l_row : 0.0f;
 #pragma unroll
-      for (int c = 0; c < HD / 32; c++) {
-        uint32_t rr[32];
+      for (int c = 0; c < HD / CW; c++) {
+        const int col = g * HD + c * CW;
+        uint32_t rr[CW];
         if (pt.n_kv > 0) {
-          tmem_ld32(t_o + lane_off + g * HD + c * 32, rr);
+          tmem_ld_n<CW>(t_o + lane_off + col, rr);
           tmem_wait_ld_regs(rr);
         } else {
 #pragma unroll
-          for (int e = 0; e < 32; e++) rr[e] = 0u;
+          for (int e = 0; e < CW; e++) rr[e] = 0u;
         }
-        uint8_t* orow = smem + C::kOffQ + (g * (HD / 32) + c) * (kBM * 128) + r * 128;
+        uint8_t* orow = buf_row(col);
 #pragma unroll
-        for (int e = 0; e < 8; e++)
-          *reinterpret_cast<float4*>(orow + ((e ^ (r & 7)) << 4)) = make_float4(
+        for (int e = 0; e < CW / 4; e++)
+          *reinterpret_cast<float4*>(orow + buf_unit(col, e)) = make_float4(
               __uint_as_float(rr[4 * e]) * inv_l, __uint_as_float(rr[4 * e + 1]) * inv_l,
               __uint_as_float(rr[4 * e + 2]) * inv_l, __uint_as_float(rr[4 * e + 3]) * inv_l);
       }
@@ -957,34 +972,34 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPair, 1)
       return true;
     };
     int G = 0, it = 0;
-    // (a failure only skips the remaining work; both warps of a quarter pair
-    // still meet at their per-block and epilogue barriers)
+    // (a failure only skips the remaining work; the warps of a quarter still
+    // meet at their per-block and epilogue barriers)
     for (int k = 0; k * n_clusters < n_work; k++) {
       const int w = work_of(k);
       if (w >= n_work) continue;
       const Tile t = tile_of(w);
       const long long qg = p.q_offset + t.q0 + r;
-      // Stage this tile's Q from the shared-memory buffer (128B-swizzled rows:
-      // 16-byte unit u of row r sits at unit u ^ (r & 7), so 32 threads reading
-      // one unit of 32 rows hit every bank).  The previous tile's QK^T MMAs are
-      // complete: its last S was visible before its last P was written.
+      // Stage this tile's Q from the shared-memory buffer.  The previous tile's
+      // QK^T MMAs are complete: its last S was visible before its last P was
+      // written.
       const bool okq =
           ok && __all_sync(0xffffffffu, mbar_wait(bar_q_smem_full, it & 1, abort_flag, p.err));
       if (lane == 0 && quarter == 0 && g == 0) FA_EV(14, G);
       if (okq) {
 #pragma unroll
-        for (int c = 0; c < HD / 32; c++) {
-          const uint8_t* qrow = smem + C::kOffQ + (g * (HD / 32) + c) * (kBM * 128) + r * 128;
-          uint32_t rr[32];
+        for (int c = 0; c < HD / CW; c++) {
+          const int col = g * HD + c * CW;
+          const uint8_t* qrow = buf_row(col);
+          uint32_t rr[CW];
 #pragma unroll
-          for (int e = 0; e < 8; e++) {
-            const float4 v4 = *reinterpret_cast<const float4*>(qrow + ((e ^ (r & 7)) << 4));
+          for (int e = 0; e < CW / 4; e++) {
+            const float4 v4 = *reinterpret_cast<const float4*>(qrow + buf_unit(col, e));
             rr[4 * e + 0] = to_tf32_rna(v4.x * c_log2);
             rr[4 * e + 1] = to_tf32_rna(v4.y * c_log2);
             rr[4 * e + 2] = to_tf32_rna(v4.z * c_log2);
             rr[4 * e + 3] = to_tf32_rna(v4.w * c_log2);
           }
-          tmem_st32(t_q + lane_off + g * HD + c * 32, rr);
+          tmem_st_n<CW>(t_q + lane_off + col, rr);
         }
         tmem_wait_st();
         tc_fence_before();
@@ -1009,7 +1024,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPair, 1)
         const int Gj = G + j, b = Gj & 1;
         const bool wt =
             __all_sync(0xffffffffu, mbar_wait(bar_s_full(b), (Gj >> 1) & 1, abort_flag, p.err));
-        if (lane == 0 && quarter == 0) FA_EV(5 + 3 * g, Gj);
+        if (lane == 0 && quarter == 0 && g < 2) FA_EV(5 + 3 * g, Gj);
         tc_fence_after();
         float x[HC];
         if (wt) {
@@ -1044,18 +1059,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPair, 1)
           mx[q] = fmax3(mx[q], x[e + 6], x[e + 7]);
         }
         const float mx_half = fmax3(mx[0], mx[1], fmaxf(mx[2], mx[3]));
-        float* slot = red + (Gj & 1) * 256;
+        float* slot = red + (Gj & 1) * (NG * 128);
         slot[g * 128 + r] = mx_half;
-        // Only the two warps holding the same 32 rows (warps 4+q and 8+q, on the
-        // same scheduler) exchange halves, through named barrier 1+q; the OR makes
-        // both leave the loop together on a failure.
-        if (bar_any(1 + quarter, 64, !wt)) {
+        // Only the NG warps holding the same 32 rows (on the same scheduler)
+        // exchange parts, through named barrier 1+q; the OR makes all of them
+        // leave the loop together on a failure.
+        if (bar_any(1 + quarter, 32 * NG, !wt)) {
           ok = false;
           break;
         }
-        if (lane == 0 && quarter == 0) FA_EV(6 + 3 * g, Gj);
-        const float mx_row = fmaxf(mx_half, slot[(g ^ 1) * 128 + r]);
-        // Both halves hold the same m and see the same mx_row, so they take
+        if (lane == 0 && quarter == 0 && g < 2) FA_EV(6 + 3 * g, Gj);
+        float mx_row = mx_half;
+#pragma unroll
+        for (int i = 0; i < NG; i++) mx_row = fmaxf(mx_row, slot[i * 128 + r]);
+        // All parts hold the same m and see the same mx_row, so they take
         // identical rescale decisions.
         const float m_new = fmaxf(m, mx_row);
         float corr = 1.0f;
@@ -1073,43 +1090,46 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsPair, 1)
           // next block's bar_any)
           tc_fence_after();
 #pragma unroll
-          for (int c = 0; c < HD / 32; c++) {
-            uint32_t rr[32];
-            tmem_ld32(t_o + lane_off + g * HD + c * 32, rr);
+          for (int c = 0; c < HD / CW; c++) {
+            uint32_t rr[CW];
+            tmem_ld_n<CW>(t_o + lane_off + g * HD + c * CW, rr);
             tmem_wait_ld_regs(rr);
 #pragma unroll
-            for (int e = 0; e < 32; e++) rr[e] = __float_as_uint(__uint_as_float(rr[e]) * corr);
-            tmem_st32(t_o + lane_off + g * HD + c * 32, rr);
+            for (int e = 0; e < CW; e++) rr[e] = __float_as_uint(__uint_as_float(rr[e]) * corr);
+            tmem_st_n<CW>(t_o + lane_off + g * HD + c * CW, rr);
           }
           l *= corr;
         }
         // p = 2^(s - m): s is already scaled by scale*log2e through Q, and m is
         // one of the row's scores, so the row's maximum gives exactly 2^0.
         const float neg_m = (m == -INFINITY) ? 0.0f : -m;
-        float2 rs2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
-        const float2 nm2 = make_float2(neg_m, neg_m);
+        // One add, one MUFU exponential, one mask and one add per score: the
+        // fewest issue slots (packed f32x2 forms and an FMA-pipe polynomial for
+        // part of the exponentials measured slower here).
+        float rs[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int c = 0; c < HC / 32; c++) {
           uint32_t rr[32];
 #pragma unroll
-          for (int e = 0; e < 32; e += 2) {
-            const float2 a = add2_rn(make_float2(x[c * 32 + e], x[c * 32 + e + 1]), nm2);
-            // half of the pairs on the FMA pipe, half on MUFU
-            const float2 pe = ((e >> 1) & 1) ? ex2_poly2(a) : make_float2(ex2(a.x), ex2(a.y));
-            const uint32_t t0 = __float_as_uint(pe.x) & 0xFFFFE000u;
-            const uint32_t t1 = __float_as_uint(pe.y) & 0xFFFFE000u;
-            rs2[(e >> 1) & 1] = add2_rn(rs2[(e >> 1) & 1],
-                                        make_float2(__uint_as_float(t0), __uint_as_float(t1)));
-            rr[e] = t0;
-            rr[e + 1] = t1;
+          for (int e = 0; e < 32; e += 8) {
+            float pe[8];
+#pragma unroll
+            for (int u = 0; u < 8; u++) pe[u] = ex2(__fadd_rn(x[c * 32 + e + u], neg_m));
+#pragma unroll
+            for (int u = 0; u < 8; u++) {
+              const uint32_t tb = __float_as_uint(pe[u]) & 0xFFFFE000u;
+              rs[u & 3] += __uint_as_float(tb);
+              rr[e + u] = tb;
+            }
           }
           tmem_st32(t_s(b) + lane_off + g * HC + c * 32, rr);
         }
-        l += (rs2[0].x + rs2[1].x) + (rs2[0].y + rs2[1].y);
+        l += (rs[0] + rs[1]) + (rs[2] + rs[3]);
+
         tmem_wait_st();
         tc_fence_before();
         warp_arrive_leader(bar_p_full(b));
-        if (lane == 0 && quarter == 0) FA_EV(7 + 3 * g, Gj);
+        if (lane == 0 && quarter == 0 && g < 2) FA_EV(7 + 3 * g, Gj);
       }
       G += t.n_kv;
       have_prev = true;
@@ -1174,9 +1194,9 @@ cudaError_t launch_tf32(const FwdParams& p, cudaStream_t s) {
   return cudaGetLastError();
 }
 
-template <int D, int BK, int NKS, int NVS>
+template <int D, int BK, int NKS, int NVS, int NG>
 cudaError_t launch_tf32_pair(const FwdParams& p, cudaStream_t s) {
-  using C = PairCfg<D, BK, NKS, NVS>;
+  using C = PairCfg<D, BK, NKS, NVS, NG>;
   CUtensorMap mk, mv;
   CUtensorMap mq, mo;
   if (!make_map(&mk, p.k, D, p.sk, p.bh, BK / 2, CU_TENSOR_MAP_SWIZZLE_128B) ||
@@ -1190,7 +1210,7 @@ cudaError_t launch_tf32_pair(const FwdParams& p, cudaStream_t s) {
   cudaGetDevice(&dev);
   const unsigned long long bit = 1ull << (dev & 63);
   if (!(attr_set.load() & bit)) {
-    cudaError_t e = cudaFuncSetAttribute(tc_fwd_tf32_pair<D, BK, NKS, NVS>,
+    cudaError_t e = cudaFuncSetAttribute(tc_fwd_tf32_pair<D, BK, NKS, NVS, NG>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          C::kSmemBytes);
     if (e == cudaSuccess)
@@ -1203,7 +1223,7 @@ cudaError_t launch_tf32_pair(const FwdParams& p, cudaStream_t s) {
   // persistent: one cluster (2 SMs) per SM pair, at most one per work tile
   const int n_clusters = (int)(n_work < sm_count[dev & 63] / 2 ? n_work : sm_count[dev & 63] / 2);
   if (n_work > INT32_MAX) return cudaErrorInvalidValue;
-  tc_fwd_tf32_pair<D, BK, NKS, NVS><<<dim3(2 * n_clusters), kThreadsPair, C::kSmemBytes, s>>>(
+  tc_fwd_tf32_pair<D, BK, NKS, NVS, NG><<<dim3(2 * n_clusters), pair_threads(NG), C::kSmemBytes, s>>>(
       mk, mv, mq, mo, p, n_pairs);
   count_launch();
   return cudaGetLastError();
@@ -1233,6 +1253,9 @@ size_t tc_scratch_floats(const FwdParams&, int) { return 0; }
 cudaError_t launch_tc(const FwdParams& p, int precision, float*, size_t, cudaStream_t s) {
   if (precision != 0) return cudaErrorInvalidValue;
   if (p.sq > 65535 * kBM) return cudaErrorInvalidValue;
+#ifndef FA_PAIR_NG
+#define FA_PAIR_NG 2
+#endif
 #ifndef FA_D128_VK
 #define FA_D128_VK 64
 #define FA_D128_NVS 3
@@ -1241,9 +1264,9 @@ cudaError_t launch_tc(const FwdParams& p, int precision, float*, size_t, cudaStr
   const bool single = p.sq <= kBM;
   if (p.d == 128)
     return single ? launch_tf32<128, 128, FA_D128_VK, 2, FA_D128_NVS>(p, s)
-                  : launch_tf32_pair<128, 128, 2, 2>(p, s);
+                  : launch_tf32_pair<128, 128, 2, 2, FA_PAIR_NG>(p, s);
   if (p.d == 64)
-    return single ? launch_tf32<64, 128, 128, 3, 3>(p, s) : launch_tf32_pair<64, 128, 3, 3>(p, s);
+    return single ? launch_tf32<64, 128, 128, 3, 3>(p, s) : launch_tf32_pair<64, 128, 3, 3, FA_PAIR_NG>(p, s);
   return cudaErrorInvalidValue;
 }
 

@@ -174,6 +174,37 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
       FA_W8(0), FA_W8(8), FA_W8(16), FA_W8(24)
       : "memory");
 }
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : FA_R8(0), FA_R8(8)
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      FA_W8(0), FA_W8(8)
+      : "memory");
+}
+// N (16 or 32) consecutive TMEM columns of this thread's lane.
+template <int N>
+__device__ __forceinline__ void tmem_ld_n(uint32_t taddr, uint32_t (&r)[N]) {
+  static_assert(N == 16 || N == 32, "16 or 32 columns");
+  if constexpr (N == 32)
+    tmem_ld32(taddr, r);
+  else
+    tmem_ld16(taddr, r);
+}
+template <int N>
+__device__ __forceinline__ void tmem_st_n(uint32_t taddr, const uint32_t (&r)[N]) {
+  static_assert(N == 16 || N == 32, "16 or 32 columns");
+  if constexpr (N == 32)
+    tmem_st32(taddr, r);
+  else
+    tmem_st16(taddr, r);
+}
 __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
@@ -194,52 +225,6 @@ __device__ __forceinline__ uint32_t to_tf32_rna(float x) {
   uint32_t r;
   asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
   return r;
-}
-// Packed two-lane f32 multiply / add (sm_100), each lane rounded to nearest.
-__device__ __forceinline__ float2 mul2_rn(float2 a, float2 b) {
-  unsigned long long r;
-  asm("mul.rn.f32x2 %0, %1, %2;"
-      : "=l"(r)
-      : "l"(*reinterpret_cast<unsigned long long*>(&a)), "l"(*reinterpret_cast<unsigned long long*>(&b)));
-  return *reinterpret_cast<float2*>(&r);
-}
-__device__ __forceinline__ float2 add2_rn(float2 a, float2 b) {
-  unsigned long long r;
-  asm("add.rn.f32x2 %0, %1, %2;"
-      : "=l"(r)
-      : "l"(*reinterpret_cast<unsigned long long*>(&a)), "l"(*reinterpret_cast<unsigned long long*>(&b)));
-  return *reinterpret_cast<float2*>(&r);
-}
-__device__ __forceinline__ float2 fma2_rn(float2 a, float2 b, float2 c) {
-  unsigned long long r;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;"
-      : "=l"(r)
-      : "l"(*reinterpret_cast<unsigned long long*>(&a)), "l"(*reinterpret_cast<unsigned long long*>(&b)),
-        "l"(*reinterpret_cast<unsigned long long*>(&c)));
-  return *reinterpret_cast<float2*>(&r);
-}
-// 2^x for two lanes on the FMA pipe (x <= 64, -inf allowed), so the softmax
-// is not limited by the MUFU unit (16 ex2 per clock per SM).  Cody-Waite
-// split x = j + f with j = round(x) (1.5*2^23 rounding trick) and f in
-// [-0.5, 0.5]; 2^f from a degree-4 polynomial fitted for this library
-// (weighted least squares towards minimax on [-0.5, 0.5]; max relative error
-// 2.7e-6 in f32); 2^j added to the exponent field.  x is clamped at -126 so
-// the exponent field stays >= 0 (2^-126 is far below the TF32 resolution of
-// the probabilities this feeds).
-__device__ __forceinline__ float2 ex2_poly2(float2 a) {
-  const float2 x = make_float2(fmaxf(a.x, -126.0f), fmaxf(a.y, -126.0f));
-  const float2 magic = make_float2(12582912.0f, 12582912.0f);
-  const float2 t = add2_rn(x, magic);
-  const float2 j = add2_rn(t, make_float2(-12582912.0f, -12582912.0f));
-  const float2 f = fma2_rn(j, make_float2(-1.0f, -1.0f), x);
-  float2 p = fma2_rn(f, make_float2(0.00957009568810463f, 0.00957009568810463f),
-                     make_float2(0.05591786280274391f, 0.05591786280274391f));
-  p = fma2_rn(p, f, make_float2(0.240247443318367f, 0.240247443318367f));
-  p = fma2_rn(p, f, make_float2(0.6931217908859253f, 0.6931217908859253f));
-  p = fma2_rn(p, f, make_float2(0.9999992847442627f, 0.9999992847442627f));
-  // (bits(t) << 23) == j << 23 modulo 2^32 because bits(1.5*2^23) << 23 == 0
-  return make_float2(__int_as_float(__float_as_int(p.x) + (__float_as_int(t.x) << 23)),
-                     __int_as_float(__float_as_int(p.y) + (__float_as_int(t.y) << 23)));
 }
 __device__ __forceinline__ float ex2(float x) {
   float y;
