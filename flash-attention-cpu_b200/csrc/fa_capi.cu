@@ -11,6 +11,8 @@
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <vector>
+#include <algorithm>
 
 namespace fa {
 namespace {
@@ -212,6 +214,129 @@ int host_streams(int dev, cudaStream_t** out) {
   return FA_OK;
 }
 
+// Host-slice forward with pageable buffers: every byte moves through the
+// library's pinned rings (fa_host_stage.cu).  Per chunk of (batch, head)
+// slices the host threads copy its Q, K, V pieces into free input slots and
+// the copy engine moves each slot to HBM; the chunk's kernel runs once its
+// inputs are in; its O (and LSE) pieces come back into output slots and the
+// host threads copy them out once their event has completed.  So the host
+// copies of one chunk overlap the transfers and the kernel of the others.
+int host_forward_staged(const float* q, const float* k, const float* v, size_t bh, size_t sq,
+                        size_t sk, size_t d, int causal, float* out, float* lse, int dev,
+                        cudaStream_t s_in, cudaStream_t s_comp, cudaStream_t s_out) {
+  fa::PinnedRing *rin = nullptr, *rout = nullptr;
+  std::mutex* call = nullptr;
+  cudaError_t e = fa::staging_acquire(dev, &rin, &rout, &call);
+  if (e != cudaSuccess) return cuda_err(e, "pinned staging buffers");
+  std::lock_guard<std::mutex> unlock(*call, std::adopt_lock);
+  const size_t nq = bh * sq * d, nk = bh * sk * d, nl = bh * sq;
+  const size_t bytes = (2 * nq + 2 * nk + nl) * sizeof(float);
+  char* buf = nullptr;
+  e = cudaMallocAsync((void**)&buf, bytes, s_in);
+  if (e != cudaSuccess) return cuda_err(e, "cudaMallocAsync(staging)");
+  float* dq = (float*)buf;
+  float* dk = dq + nq;
+  float* dv = dk + nk;
+  float* dout = dv + nk;
+  float* dlse = dout + nq;
+  constexpr size_t kSlot = fa::PinnedRing::kSlotBytes;
+  struct Piece {
+    int slot;
+    char* dst;
+    size_t n;
+  };
+  std::vector<Piece> pend;  // output pieces in flight, oldest first
+  size_t pend_head = 0;
+  auto drain_one = [&]() -> cudaError_t {
+    const Piece pc = pend[pend_head++];
+    cudaError_t r = cudaEventSynchronize(rout->ev[pc.slot]);
+    if (r == cudaSuccess) fa::parallel_copy(pc.dst, rout->buf[pc.slot], pc.n);
+    rout->busy[pc.slot] = false;
+    return r;
+  };
+  auto stage_in = [&](float* dst, const float* src, size_t n_bytes) -> cudaError_t {
+    for (size_t off = 0; off < n_bytes; off += kSlot) {
+      const size_t n = std::min(kSlot, n_bytes - off);
+      const int sl = rin->next;
+      rin->next = (sl + 1) % fa::PinnedRing::kSlots;
+      if (rin->busy[sl]) {
+        cudaError_t r = cudaEventSynchronize(rin->ev[sl]);
+        if (r != cudaSuccess) return r;
+      }
+      fa::parallel_copy(rin->buf[sl], (const char*)src + off, n);
+      cudaError_t r = cudaMemcpyAsync((char*)dst + off, rin->buf[sl], n, cudaMemcpyHostToDevice, s_in);
+      if (r == cudaSuccess) r = cudaEventRecord(rin->ev[sl], s_in);
+      if (r != cudaSuccess) return r;
+      rin->busy[sl] = true;
+    }
+    return cudaSuccess;
+  };
+  auto stage_out = [&](float* dst, const float* src, size_t n_bytes) -> cudaError_t {
+    for (size_t off = 0; off < n_bytes; off += kSlot) {
+      const size_t n = std::min(kSlot, n_bytes - off);
+      const int sl = rout->next;
+      rout->next = (sl + 1) % fa::PinnedRing::kSlots;
+      while (rout->busy[sl]) {
+        cudaError_t r = drain_one();
+        if (r != cudaSuccess) return r;
+      }
+      cudaError_t r = cudaMemcpyAsync(rout->buf[sl], (const char*)src + off, n, cudaMemcpyDeviceToHost, s_out);
+      if (r == cudaSuccess) r = cudaEventRecord(rout->ev[sl], s_out);
+      if (r != cudaSuccess) return r;
+      rout->busy[sl] = true;
+      pend.push_back({sl, (char*)dst + off, n});
+    }
+    return cudaSuccess;
+  };
+  // about 16 chunks, so that the first inputs and the last outputs (which
+  // nothing overlaps) are short
+  const size_t n_chunks = bh < 16 ? bh : 16;
+  const size_t per = (bh + n_chunks - 1) / n_chunks;
+  cudaEvent_t ev_in = nullptr, ev_comp = nullptr;
+  e = cudaEventCreateWithFlags(&ev_in, cudaEventDisableTiming);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ev_comp, cudaEventDisableTiming);
+  int rc = FA_OK;
+  for (size_t h0 = 0; h0 < bh && e == cudaSuccess && rc == FA_OK; h0 += per) {
+    const size_t h1 = (h0 + per < bh) ? h0 + per : bh;
+    const size_t oq = h0 * sq * d, ok_ = h0 * sk * d, cq = (h1 - h0) * sq * d,
+                 ck = (h1 - h0) * sk * d;
+    e = stage_in(dq + oq, q + oq, cq * sizeof(float));
+    if (e == cudaSuccess) e = stage_in(dk + ok_, k + ok_, ck * sizeof(float));
+    if (e == cudaSuccess) e = stage_in(dv + ok_, v + ok_, ck * sizeof(float));
+    if (e == cudaSuccess) e = cudaEventRecord(ev_in, s_in);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(s_comp, ev_in, 0);
+    if (e != cudaSuccess) break;
+    fa::FwdParams p{};
+    p.q = dq + oq; p.k = dk + ok_; p.v = dv + ok_; p.o = dout + oq;
+    p.lse = lse ? dlse + h0 * sq : nullptr;
+    p.bh = (int)(h1 - h0); p.sq = (int)sq; p.sk = (int)sk; p.d = (int)d;
+    p.q_offset = 0; p.k_offset = 0; p.causal = causal ? 1 : 0;
+    rc = dispatch(p, dev, s_comp);
+    if (rc != FA_OK) break;
+    e = cudaEventRecord(ev_comp, s_comp);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(s_out, ev_comp, 0);
+    if (e == cudaSuccess) e = stage_out(out + oq, dout + oq, cq * sizeof(float));
+    if (e == cudaSuccess && lse)
+      e = stage_out(lse + h0 * sq, dlse + h0 * sq, (h1 - h0) * sq * sizeof(float));
+    // copy out whatever has already come back
+    while (e == cudaSuccess && pend_head < pend.size() &&
+           cudaEventQuery(rout->ev[pend[pend_head].slot]) == cudaSuccess)
+      e = drain_one();
+  }
+  while (e == cudaSuccess && pend_head < pend.size()) e = drain_one();
+  cudaStreamSynchronize(s_out);
+  cudaStreamSynchronize(s_comp);
+  cudaStreamSynchronize(s_in);
+  for (size_t i = pend_head; i < pend.size(); i++) rout->busy[pend[i].slot] = false;
+  if (rc == FA_OK && e != cudaSuccess) rc = cuda_err(e, "pinned staging");
+  if (rc == FA_OK) rc = check_err_flag(dev, s_in);
+  cudaFreeAsync(buf, s_in);
+  cudaStreamSynchronize(s_in);
+  if (ev_in) cudaEventDestroy(ev_in);
+  if (ev_comp) cudaEventDestroy(ev_comp);
+  return rc;
+}
+
 // Host-slice forward: stage to HBM, run, copy back, check.
 int host_forward(const float* q, const float* k, const float* v, size_t bh, size_t sq,
                  size_t sk, size_t d, int causal, float* out, float* lse) {
@@ -225,6 +350,12 @@ int host_forward(const float* q, const float* k, const float* v, size_t bh, size
   cudaStream_t s_in = st[0], s_comp = st[1], s_out = st[2];
   const size_t nq = bh * sq * d, nk = bh * sk * d, nl = bh * sq;
   const size_t bytes = (2 * nq + 2 * nk + nl) * sizeof(float);
+  // Pageable buffers of a large call go through the pinned rings.
+  if (bytes >= (size_t(16) << 20) &&
+      (fa::is_pageable(q) || fa::is_pageable(k) || fa::is_pageable(v) ||
+       fa::is_pageable(out) || (lse && fa::is_pageable(lse))))
+    return host_forward_staged(q, k, v, bh, sq, sk, d, causal, out, lse, dev, s_in, s_comp,
+                               s_out);
   const size_t n_chunks = (bh >= 2 && bytes >= (size_t(32) << 20)) ? (bh < 8 ? bh : 8) : 1;
   const size_t per = (bh + n_chunks - 1) / n_chunks;
   char* buf = nullptr;
@@ -497,6 +628,7 @@ uint64_t fa_launch_count(void) { return fa::launches_issued(); }
 const char* fa_last_path(void) { return t_path; }
 
 void fa_shutdown(void) {
+  fa::staging_release_all();
   for (int d = 0; d < kMaxDevices; d++)
     for (int i = 0; i < 3; i++)
       if (t_streams.s[d][i]) {

@@ -1,6 +1,7 @@
 // Shared definitions of the B200 attention-forward kernels.
 #pragma once
 #include <cuda_runtime.h>
+#include <mutex>
 #include <stdint.h>
 
 namespace fa {
@@ -83,4 +84,24 @@ size_t tc3_workspace_floats(const FwdParams& p);
 cudaError_t launch_tc3(const FwdParams& p, float* ws, cudaStream_t s);
 unsigned long long launches_issued();
 void count_launch(int n = 1);
+
+// Host staging for host-slice calls with pageable buffers (fa_host_stage.cu).
+// A ring of pinned slots: a slot is reused after its event (recorded after the
+// copy that reads or writes it) has completed.
+struct PinnedRing {
+  static constexpr int kSlots = 4;
+  static constexpr size_t kSlotBytes = size_t(16) << 20;
+  char* buf[kSlots] = {};
+  cudaEvent_t ev[kSlots] = {};
+  bool busy[kSlots] = {};
+  int next = 0;
+};
+// memcpy split over a fixed pool of host threads (single-threaded below 4 MB).
+void parallel_copy(void* dst, const void* src, size_t bytes);
+// true for memory the copy engines cannot read directly (not pinned or registered)
+bool is_pageable(const void* p);
+// Locks the device's staging rings (allocated on first use) for one call; the
+// caller unlocks *call when done.
+cudaError_t staging_acquire(int dev, PinnedRing** in, PinnedRing** out, std::mutex** call);
+void staging_release_all();
 }  // namespace fa

@@ -1,0 +1,166 @@
+// Host-side staging for the host-slice calls made with pageable buffers (the
+// crate's `&[f32]` / `&mut [f32]` are ordinary heap memory).  A copy engine
+// reads pageable memory only through the driver's own bounce buffers, which
+// runs at a fraction of the PCIe rate, so such a call instead goes through
+// rings of pinned slots that the library owns: host threads copy a piece of
+// the input into a slot while the copy engine moves the previous slot to the
+// device, and outputs come back the same way in reverse.
+#include "fa_common.cuh"
+
+#include <algorithm>
+#include <condition_variable>
+#include <cstring>
+#include <mutex>
+#include <thread>
+#include <vector>
+
+namespace fa {
+namespace {
+
+// A fixed pool of worker threads for one large memcpy at a time: the caller
+// takes the first part, each worker one of the others.
+class CopyPool {
+ public:
+  CopyPool() {
+    const unsigned hw = std::thread::hardware_concurrency();
+    n_ = (int)std::min(16u, std::max(1u, hw));
+    for (int i = 1; i < n_; i++) workers_.emplace_back([this, i] { run(i); });
+  }
+  ~CopyPool() {
+    {
+      std::lock_guard<std::mutex> lk(m_);
+      stop_ = true;
+    }
+    cv_.notify_all();
+    for (auto& t : workers_) t.join();
+  }
+  void copy(char* dst, const char* src, size_t bytes) {
+    if (n_ == 1 || bytes < (size_t(4) << 20)) {
+      std::memcpy(dst, src, bytes);
+      return;
+    }
+    std::lock_guard<std::mutex> call(call_m_);  // one parallel copy at a time
+    {
+      std::lock_guard<std::mutex> lk(m_);
+      dst_ = dst;
+      src_ = src;
+      bytes_ = bytes;
+      pending_ = n_ - 1;
+      gen_++;
+    }
+    cv_.notify_all();
+    part(0);
+    std::unique_lock<std::mutex> lk(m_);
+    done_cv_.wait(lk, [this] { return pending_ == 0; });
+  }
+
+ private:
+  void part(int i) {
+    // 64-byte aligned split points
+    const size_t per = ((bytes_ + n_ - 1) / n_ + 63) & ~size_t(63);
+    const size_t a = std::min(bytes_, per * i), b = std::min(bytes_, a + per);
+    if (b > a) std::memcpy(dst_ + a, src_ + a, b - a);
+  }
+  void run(int i) {
+    unsigned long long seen = 0;
+    for (;;) {
+      {
+        std::unique_lock<std::mutex> lk(m_);
+        cv_.wait(lk, [&] { return stop_ || gen_ != seen; });
+        if (stop_) return;
+        seen = gen_;
+      }
+      part(i);
+      {
+        std::lock_guard<std::mutex> lk(m_);
+        if (--pending_ == 0) done_cv_.notify_one();
+      }
+    }
+  }
+  int n_ = 1;
+  std::vector<std::thread> workers_;
+  std::mutex m_, call_m_;
+  std::condition_variable cv_, done_cv_;
+  bool stop_ = false;
+  unsigned long long gen_ = 0;
+  int pending_ = 0;
+  char* dst_ = nullptr;
+  const char* src_ = nullptr;
+  size_t bytes_ = 0;
+};
+
+CopyPool& copy_pool() {
+  static CopyPool pool;
+  return pool;
+}
+
+struct Rings {
+  std::mutex call;  // one staged call per device at a time
+  bool ready = false;
+  PinnedRing in, out;
+};
+Rings g_rings[64];
+
+}  // namespace
+
+void parallel_copy(void* dst, const void* src, size_t bytes) {
+  copy_pool().copy(static_cast<char*>(dst), static_cast<const char*>(src), bytes);
+}
+
+bool is_pageable(const void* p) {
+  cudaPointerAttributes a;
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    cudaGetLastError();
+    return true;
+  }
+  return a.type == cudaMemoryTypeUnregistered;
+}
+
+static cudaError_t ring_init(PinnedRing& r) {
+  for (int i = 0; i < PinnedRing::kSlots; i++) {
+    cudaError_t e = cudaMallocHost((void**)&r.buf[i], PinnedRing::kSlotBytes);
+    if (e != cudaSuccess) return e;
+    e = cudaEventCreateWithFlags(&r.ev[i], cudaEventDisableTiming);
+    if (e != cudaSuccess) return e;
+    r.busy[i] = false;
+  }
+  r.next = 0;
+  return cudaSuccess;
+}
+
+cudaError_t staging_acquire(int dev, PinnedRing** in, PinnedRing** out, std::mutex** call) {
+  Rings& g = g_rings[dev & 63];
+  *call = &g.call;
+  g.call.lock();
+  if (!g.ready) {
+    cudaError_t e = ring_init(g.in);
+    if (e == cudaSuccess) e = ring_init(g.out);
+    if (e != cudaSuccess) {
+      g.call.unlock();
+      return e;
+    }
+    g.ready = true;
+  }
+  *in = &g.in;
+  *out = &g.out;
+  return cudaSuccess;
+}
+
+void staging_release_all() {
+  for (int d = 0; d < 64; d++) {
+    Rings& g = g_rings[d];
+    std::lock_guard<std::mutex> lk(g.call);
+    if (!g.ready) continue;
+    cudaSetDevice(d);
+    for (PinnedRing* r : {&g.in, &g.out})
+      for (int i = 0; i < PinnedRing::kSlots; i++) {
+        cudaEventSynchronize(r->ev[i]);
+        cudaEventDestroy(r->ev[i]);
+        cudaFreeHost(r->buf[i]);
+        r->buf[i] = nullptr;
+      }
+    g.ready = false;
+  }
+}
+
+}  // namespace fa

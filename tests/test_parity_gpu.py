@@ -335,3 +335,26 @@ def test_partial_ranges_with_keyless_tiles(fa):
     fa.sync_status()
     assert max_abs_diff(out.cpu().numpy().ravel(), want) < 2e-3
     assert max_abs_diff(lse.cpu().numpy().ravel(), wlse) < 2e-3
+
+
+@pytest.mark.parametrize("prec", [0, 1])
+def test_pageable_host_buffers_go_through_pinned_staging(fa, prec):
+    # A call this large with ordinary (pageable) numpy buffers takes the pinned
+    # staging path; it must give exactly what the device API gives.
+    import torch
+    fa.set_precision(prec)
+    bh, s, d = 12, 1024, 128
+    q, k, v = (random_vec(bh * s * d, 71), random_vec(bh * s * d, 72),
+               random_vec(bh * s * d, 73))
+    out, lse = fa.multihead_lse(q, k, v, bh, s, s, d, True)
+    dq, dk, dv = (torch.from_numpy(x).cuda().view(bh, s, d) for x in (q, k, v))
+    dout = torch.empty_like(dq)
+    dlse = torch.empty(bh, s, device="cuda")
+    fa.forward_device(dq, dk, dv, dout, dlse, causal=True)
+    fa.sync_status()
+    assert np.array_equal(out, dout.cpu().numpy().ravel())
+    assert np.array_equal(lse, dlse.cpu().numpy().ravel())
+    out2 = np.zeros(bh * s * d, np.float32)
+    fa.flash_attention_multihead_v2(q, k, v, 1, bh, s, s, d, fa.FlashAttentionConfig(64, 128, True),
+                                    out2)
+    assert np.array_equal(out2, out)
