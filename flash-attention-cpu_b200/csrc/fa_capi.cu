@@ -627,6 +627,32 @@ const char* fa_last_error(void) { return t_err.c_str(); }
 uint64_t fa_launch_count(void) { return fa::launches_issued(); }
 const char* fa_last_path(void) { return t_path; }
 
+int fa_pin_host(void* ptr, size_t bytes) {
+  t_err.clear();
+  if (!ptr || bytes == 0) return set_err(FA_ERR_ARG, "null or empty host range");
+  int dev = 0;
+  int rc = prepare_device(&dev);
+  if (rc) return rc;
+  cudaError_t e = cudaHostRegister(ptr, bytes, cudaHostRegisterDefault);
+  if (e == cudaErrorHostMemoryAlreadyRegistered) {
+    cudaGetLastError();
+    return FA_OK;
+  }
+  if (e != cudaSuccess) return cuda_err(e, "cudaHostRegister");
+  return FA_OK;
+}
+
+int fa_unpin_host(void* ptr) {
+  t_err.clear();
+  if (!ptr) return set_err(FA_ERR_ARG, "null host pointer");
+  int dev = 0;
+  int rc = prepare_device(&dev);
+  if (rc) return rc;
+  cudaError_t e = cudaHostUnregister(ptr);
+  if (e != cudaSuccess) return cuda_err(e, "cudaHostUnregister");
+  return FA_OK;
+}
+
 void fa_shutdown(void) {
   fa::staging_release_all();
   for (int d = 0; d < kMaxDevices; d++)

@@ -124,6 +124,10 @@ def _load():
     L.fa_last_path.restype = ctypes.c_char_p
     L.fa_launch_count.restype = ctypes.c_uint64
     L.fa_config_default.restype = _CConfig
+    L.fa_pin_host.argtypes = [_P, _SZ]
+    L.fa_pin_host.restype = ctypes.c_int
+    L.fa_unpin_host.argtypes = [_P]
+    L.fa_unpin_host.restype = ctypes.c_int
     _lib = L
     return L
 
@@ -299,6 +303,16 @@ def device_count() -> int:
 
 def launch_count() -> int:
     return int(_load().fa_launch_count())
+
+
+def pin_host(arr) -> None:
+    """Page-lock a numpy array's memory (fa_pin_host) for fast host-slice calls."""
+    _check(_load().fa_pin_host(arr.ctypes.data, arr.nbytes))
+
+
+def unpin_host(arr) -> None:
+    """Undo pin_host for the same array."""
+    _check(_load().fa_unpin_host(arr.ctypes.data))
 
 
 def last_path() -> str:

@@ -196,6 +196,14 @@ FA_API uint64_t fa_launch_count(void);
 /* Name of the kernel family the last successful call on this thread used
  * ("tcgen05_tf32", "tcgen05_3xtf32", "simt_fp32", "decode_splitkv", ...). */
 FA_API const char* fa_last_path(void);
+/* Page-locks (pins) `bytes` of host memory at `ptr` for the copy engines, so
+ * host-slice calls on buffers inside it move data at the full PCIe rate
+ * instead of through the library's pinned staging slots.  For buffers a caller
+ * reuses across many calls.  Not in the crate's API (it has no device).
+ * Memory that is already pinned is accepted as it is. */
+FA_API int fa_pin_host(void* ptr, size_t bytes);
+/* Undoes fa_pin_host (`ptr` as given to it). */
+FA_API int fa_unpin_host(void* ptr);
 /* Frees cached device workspaces and staging buffers. */
 FA_API void fa_shutdown(void);
 
