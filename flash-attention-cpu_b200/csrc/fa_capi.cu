@@ -525,6 +525,89 @@ int fa_forward_partial_device(const float* q, const float* k, const float* v, fl
   return device_forward(q, k, v, out, lse, bh, sq, sk, d, causal, q_offset, k_offset, stream);
 }
 
+int fa_backward_device(const float* q, const float* k, const float* v, const float* out,
+                       const float* lse, const float* dout, float* dq, float* dk, float* dv,
+                       size_t bh, size_t sq, size_t sk, size_t d, int causal, void* stream) {
+  t_err.clear();
+  if (bh == 0 || sq == 0 || sk == 0 || d == 0) return FA_OK;
+  if (!q || !k || !v || !out || !lse || !dout || !dq || !dk || !dv)
+    return set_err(FA_ERR_ARG, "null buffer pointer");
+  if (d > 128) return set_err(FA_ERR_UNSUPPORTED, "backward: d_head > 128 is not supported");
+  if (bh > (size_t)INT32_MAX || sq > (size_t)INT32_MAX || sk > (size_t)INT32_MAX)
+    return set_err(FA_ERR_ARG, "dimension too large");
+  int dev = 0;
+  int rc = prepare_device(&dev);
+  if (rc) return rc;
+  cudaStream_t s = (cudaStream_t)stream;
+  fa::BwdParams p{};
+  p.q = q; p.k = k; p.v = v; p.o = out; p.lse = lse; p.dout = dout;
+  p.dq = dq; p.dk = dk; p.dv = dv;
+  p.bh = (int)bh; p.sq = (int)sq; p.sk = (int)sk; p.d = (int)d;
+  p.causal = causal ? 1 : 0;
+  p.scale = 1.0f / sqrtf((float)d);
+  float* ws = nullptr;
+  cudaError_t e = cudaMallocAsync((void**)&ws, fa::bwd_workspace_floats(p) * sizeof(float), s);
+  if (e != cudaSuccess) return cuda_err(e, "cudaMallocAsync(backward workspace)");
+  e = fa::launch_bwd(p, ws, s);
+  cudaFreeAsync(ws, s);
+  if (e != cudaSuccess) return cuda_err(e, "backward launch");
+  t_path = "simt_backward";
+  return FA_OK;
+}
+
+int fa_flash_attention_backward(const float* q, const float* k, const float* v, const float* out,
+                                const float* lse, const float* dout, float* dq, float* dk,
+                                float* dv, size_t bh, size_t sq, size_t sk, size_t d,
+                                int causal) {
+  t_err.clear();
+  if (bh == 0 || sq == 0 || sk == 0 || d == 0) return FA_OK;
+  if (!q || !k || !v || !out || !lse || !dout || !dq || !dk || !dv)
+    return set_err(FA_ERR_ARG, "null buffer pointer");
+  size_t nq, nk;
+  if (!mul_ok(bh, sq, &nq) || !mul_ok(nq, d, &nq) || !mul_ok(bh, sk, &nk) || !mul_ok(nk, d, &nk))
+    return set_err(FA_ERR_ARG, "size overflow");
+  int dev = 0;
+  int rc = prepare_device(&dev);
+  if (rc) return rc;
+  cudaStream_t* st;
+  if ((rc = host_streams(dev, &st))) return rc;
+  cudaStream_t s = st[1];
+  const size_t nl = bh * sq;
+  const size_t floats = 4 * nq + 4 * nk + nl;  // q o do dq, k v dk dv, lse
+  float* buf = nullptr;
+  cudaError_t e = cudaMallocAsync((void**)&buf, floats * sizeof(float), s);
+  if (e != cudaSuccess) return cuda_err(e, "cudaMallocAsync(backward buffers)");
+  float *dq_ = buf, *dO = dq_ + nq, *dout_ = dO + nq, *dqo = dout_ + nq;
+  float *dk_ = dqo + nq, *dv_ = dk_ + nk, *dko = dv_ + nk, *dvo = dko + nk, *dl = dvo + nk;
+  const struct {
+    float* dst;
+    const float* src;
+    size_t n;
+  } ins[] = {{dq_, q, nq}, {dO, out, nq}, {dout_, dout, nq}, {dk_, k, nk}, {dv_, v, nk},
+             {dl, lse, nl}};
+  for (const auto& c : ins)
+    if (e == cudaSuccess)
+      e = cudaMemcpyAsync(c.dst, c.src, c.n * sizeof(float), cudaMemcpyHostToDevice, s);
+  if (e == cudaSuccess) {
+    rc = fa_backward_device(dq_, dk_, dv_, dO, dl, dout_, dqo, dko, dvo, bh, sq, sk, d, causal,
+                            s);
+    if (rc == FA_OK) {
+      e = cudaMemcpyAsync(dq, dqo, nq * sizeof(float), cudaMemcpyDeviceToHost, s);
+      if (e == cudaSuccess)
+        e = cudaMemcpyAsync(dk, dko, nk * sizeof(float), cudaMemcpyDeviceToHost, s);
+      if (e == cudaSuccess)
+        e = cudaMemcpyAsync(dv, dvo, nk * sizeof(float), cudaMemcpyDeviceToHost, s);
+    }
+  }
+  cudaError_t e2 = cudaStreamSynchronize(s);
+  cudaFreeAsync(buf, s);
+  cudaStreamSynchronize(s);
+  if (rc != FA_OK) return rc;
+  if (e == cudaSuccess) e = e2;
+  if (e != cudaSuccess) return cuda_err(e, "backward copies");
+  return FA_OK;
+}
+
 int fa_lse_combine_device(const float* o_parts, const float* lse_parts, size_t n_parts,
                           size_t rows, size_t d, float* out, float* lse_out, void* stream) {
   t_err.clear();

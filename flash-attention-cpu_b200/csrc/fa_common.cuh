@@ -24,6 +24,24 @@ struct FwdParams {
   int* err;          // device error word (0 = ok), see ErrCode
 };
 
+// Backward pass (fa_bwd.cu): gradients of the forward above.
+struct BwdParams {
+  const float* q;
+  const float* k;
+  const float* v;
+  const float* o;     // forward output
+  const float* lse;   // forward row LSE (natural log, scaled scores)
+  const float* dout;  // gradient of the output
+  float* dq;
+  float* dk;
+  float* dv;
+  float* dvec;        // workspace [bh, sq]: rowsum(dO * O)
+  int bh, sq, sk, d;
+  long long q_offset, k_offset;
+  int causal;
+  float scale;
+};
+
 enum ErrCode : int {
   kErrNone = 0,
   kErrTimeout = 1,  // a bounded mbarrier wait expired
@@ -102,6 +120,10 @@ void parallel_copy(void* dst, const void* src, size_t bytes);
 bool is_pageable(const void* p);
 // Locks the device's staging rings (allocated on first use) for one call; the
 // caller unlocks *call when done.
+size_t bwd_workspace_floats(const BwdParams& p);
+// Enqueues the three backward kernels (d_head <= 128); `dvec` is workspace of
+// bwd_workspace_floats(p) floats.
+cudaError_t launch_bwd(BwdParams p, float* dvec, cudaStream_t s);
 cudaError_t staging_acquire(int dev, PinnedRing** in, PinnedRing** out, std::mutex** call);
 void staging_release_all();
 }  // namespace fa

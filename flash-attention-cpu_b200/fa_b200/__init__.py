@@ -124,6 +124,10 @@ def _load():
     L.fa_last_path.restype = ctypes.c_char_p
     L.fa_launch_count.restype = ctypes.c_uint64
     L.fa_config_default.restype = _CConfig
+    L.fa_backward_device.argtypes = [_P] * 9 + [_SZ, _SZ, _SZ, _SZ, ctypes.c_int, _P]
+    L.fa_backward_device.restype = ctypes.c_int
+    L.fa_flash_attention_backward.argtypes = [_P] * 9 + [_SZ, _SZ, _SZ, _SZ, ctypes.c_int]
+    L.fa_flash_attention_backward.restype = ctypes.c_int
     L.fa_pin_host.argtypes = [_P, _SZ]
     L.fa_pin_host.restype = ctypes.c_int
     L.fa_unpin_host.argtypes = [_P]
@@ -303,6 +307,39 @@ def device_count() -> int:
 
 def launch_count() -> int:
     return int(_load().fa_launch_count())
+
+
+def backward_device(q, k, v, out, lse, dout, dq, dk, dv, causal=False, stream=None):
+    """Gradients dq, dk, dv of the forward (device tensors; q/out/dout/dq [bh, sq, d],
+    k/v/dk/dv [bh, sk, d], lse [bh, sq] from the forward).  Asynchronous."""
+    bh, sq, d = q.shape
+    sk = k.shape[1]
+    for name, t, shape in (("k", k, (bh, sk, d)), ("v", v, (bh, sk, d)), ("out", out, (bh, sq, d)),
+                           ("dout", dout, (bh, sq, d)), ("dq", dq, (bh, sq, d)),
+                           ("dk", dk, (bh, sk, d)), ("dv", dv, (bh, sk, d))):
+        if tuple(t.shape) != shape:
+            raise Panic(f"{name} shape mismatch")
+    _check(_load().fa_backward_device(
+        _dptr(q, "q"), _dptr(k, "k"), _dptr(v, "v"), _dptr(out, "out"), _dptr(lse, "lse"),
+        _dptr(dout, "dout"), _dptr(dq, "dq"), _dptr(dk, "dk"), _dptr(dv, "dv"),
+        bh, sq, sk, d, int(bool(causal)), _stream(stream)))
+
+
+def flash_attention_backward(q, k, v, out, lse, dout, batch_heads, seq_len_q, seq_len_k, d_head,
+                             causal=False):
+    """Host-buffer backward: returns (dq, dk, dv) as new float32 arrays."""
+    import numpy as np
+    nq, nk = batch_heads * seq_len_q * d_head, batch_heads * seq_len_k * d_head
+    arrs = [np.ascontiguousarray(a, np.float32) for a in (q, k, v, out, lse, dout)]
+    want = (nq, nk, nk, nq, batch_heads * seq_len_q, nq)
+    for name, a, n in zip(("q", "k", "v", "out", "lse", "dout"), arrs, want):
+        if a.size != n:
+            raise Panic(f"{name} shape mismatch")
+    dq, dk, dv = np.zeros(nq, np.float32), np.zeros(nk, np.float32), np.zeros(nk, np.float32)
+    _check(_load().fa_flash_attention_backward(
+        *(a.ctypes.data for a in arrs), dq.ctypes.data, dk.ctypes.data, dv.ctypes.data,
+        batch_heads, seq_len_q, seq_len_k, d_head, int(bool(causal))))
+    return dq, dk, dv
 
 
 def pin_host(arr) -> None:

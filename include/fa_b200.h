@@ -177,6 +177,24 @@ FA_API int fa_forward_decode_noalloc(const float* q, const float* k, const float
                                      float* lse, size_t batch_heads, size_t seq_len_q,
                                      size_t seq_len_k, size_t d_head, int causal, void* stream);
 
+/* ---- backward pass (no crate counterpart: the crate is forward-only) ------ */
+
+/* Gradients of the forward: given Q, K, V, the forward output O and its row
+ * LSE (from fa_flash_attention_multihead_lse / fa_forward_device) and dO,
+ * writes dQ [bh, seq_len_q, d_head], dK and dV [bh, seq_len_k, d_head].  Exact
+ * f32 on the CUDA cores, any precision setting; d_head <= 128.  Same causal
+ * convention as the forward (top-left).  Device buffers, async on `stream`. */
+FA_API int fa_backward_device(const float* q, const float* k, const float* v, const float* out,
+                              const float* lse, const float* dout, float* dq, float* dk,
+                              float* dv, size_t batch_heads, size_t seq_len_q, size_t seq_len_k,
+                              size_t d_head, int causal, void* stream);
+/* The same on host buffers (synchronous; copies in and out). */
+FA_API int fa_flash_attention_backward(const float* q, const float* k, const float* v,
+                                       const float* out, const float* lse, const float* dout,
+                                       float* dq, float* dk, float* dv, size_t batch_heads,
+                                       size_t seq_len_q, size_t seq_len_k, size_t d_head,
+                                       int causal);
+
 /* Waits for `stream` and reports whether any kernel this library enqueued on
  * the current device has hit its bounded-wait limit since the last check
  * (FA_ERR_TIMEOUT; the flag is then cleared).  The device-resident calls are

@@ -123,3 +123,35 @@ def naive_f64(q, k, v, sq, sk, d, causal, row0=0, row1=None):
     lib().oracle_naive_f64_rows(_fp(q), _fp(k), _fp(v), sq, sk, d, int(causal), row0,
                                 row1, out.ctypes.data_as(_D), lse.ctypes.data_as(_D))
     return out[: n * d], lse[:n]
+
+
+def attention_backward_f64(q, k, v, dout, sq, sk, d, causal):
+    """f64 gradients (dq, dk, dv) of softmax(scale Q K^T) V for one slice.
+
+    The reference crate has no backward pass, so this restates the calculus
+    of its forward (``src/naive.rs:14-75``: scale 1/sqrt(d), top-left causal
+    mask) directly: P = softmax(S), dV = P^T dO, dP = dO V^T,
+    dS = P * (dP - rowsum(dO * O)), dQ = scale dS K, dK = scale dS^T Q.
+    Rows that see no key have P = 0 and zero gradients.
+    """
+    Q = np.asarray(q, np.float64).reshape(sq, d)
+    K = np.asarray(k, np.float64).reshape(sk, d)
+    V = np.asarray(v, np.float64).reshape(sk, d)
+    dO = np.asarray(dout, np.float64).reshape(sq, d)
+    scale = 1.0 / np.sqrt(np.float32(d))
+    S = (Q @ K.T) * float(scale)
+    if causal:
+        S = np.where(np.arange(sk)[None, :] <= np.arange(sq)[:, None], S, -np.inf)
+    m = S.max(axis=1, keepdims=True)
+    m = np.where(np.isfinite(m), m, 0.0)
+    E = np.exp(S - m)
+    l = E.sum(axis=1, keepdims=True)
+    P = np.where(l > 0, E / np.where(l > 0, l, 1.0), 0.0)
+    O = P @ V
+    dV = P.T @ dO
+    dP = dO @ V.T
+    Dv = (dO * O).sum(axis=1, keepdims=True)
+    dS = P * (dP - Dv)
+    dQ = (dS @ K) * float(scale)
+    dK = (dS.T @ Q) * float(scale)
+    return dQ.ravel(), dK.ravel(), dV.ravel()
