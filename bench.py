@@ -339,6 +339,60 @@ def run_kv_split(args, cfg, rank, world, local, dev):
     dist.destroy_process_group()
 
 
+def run_backward(args, cfg, q, k, v, out, lse, gen, rank, world, local, dev):
+    """`--backward`: device time of fa_backward_device on the workload (forward
+    output and LSE computed once beforehand).  FLOPs are the five matmuls of the
+    gradient (S, dP, dV, dQ, dK: 2.5x the forward's count); the kernels run on
+    the CUDA cores in f32 and recompute S and dP once more for dQ."""
+    import torch
+    import torch.distributed as dist
+    import fa_b200
+    bh, sq, sk, d, causal, seed, factor, _ = cfg
+    steps = args.steps if args.steps <= 200 else 40
+    dout = torch.randn(bh, sq, d, device=dev, generator=gen) * factor
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    stream = torch.cuda.current_stream()
+    fa_b200.forward_device(q, k, v, out, lse, causal=causal, stream=stream)
+    clk = ClockSampler(local).__enter__()
+    time.sleep(0.3)
+    for _ in range(args.warmup):
+        fa_b200.backward_device(q, k, v, out, lse, dout, dq, dk, dv, causal=causal, stream=stream)
+    fa_b200.sync_status(stream)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    launches0 = fa_b200.launch_count()
+    wall0 = time.time()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        fa_b200.backward_device(q, k, v, out, lse, dout, dq, dk, dv, causal=causal, stream=stream)
+    e1.record()
+    torch.cuda.synchronize()
+    wall1 = time.time()
+    time.sleep(0.25)
+    clk.__exit__(None, None, None)
+    launches = fa_b200.launch_count() - launches0
+    fa_b200.sync_status(stream)
+    t = torch.tensor([e0.elapsed_time(e1) / steps], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.barrier()
+    step_ms = float(t.item())
+    fl = 2.5 * flops_of(bh, sq, sk, d, causal)
+    if rank == 0:
+        line = {"metric": "attention backward TFLOP/s", "value": world * fl / step_ms / 1e9,
+                "unit": "TFLOP/s", "n_gpus": world, "steps": steps, "warmup": args.warmup,
+                "ms_per_step": step_ms, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+                "config": dict(config_dict(args, cfg, world), precision="f32 (CUDA cores)"),
+                "clocks": clk.summary(wall0, wall1), "gpu_launches": launches,
+                "kernel": fa_b200.last_path()}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def config_dict(args, cfg, world):
     bh, sq, sk, d, causal, seed, factor, desc = cfg
     return {"workload": f"{args.config}: {desc}", "batch_heads_per_gpu": bh, "seq_len_q": sq,
@@ -364,6 +418,8 @@ def main():
                     help="config 5 through the key-range split even on one GPU")
     ap.add_argument("--bh", type=int, default=0,
                     help="override the slice count (smaller cases for profiler captures)")
+    ap.add_argument("--backward", action="store_true",
+                    help="time the backward pass (dQ, dK, dV) of the workload instead")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -395,6 +451,8 @@ def main():
     v = torch.randn(bh, sk, d, device=dev, generator=gen) * factor
     out = torch.empty_like(q)
     lse = torch.empty(bh, sq, device=dev)
+    if args.backward:
+        return run_backward(args, cfg, q, k, v, out, lse, gen, rank, world, local, dev)
     flush = None
     if bytes_of(bh, sq, sk, d) <= 126e6:
         flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)
