@@ -530,21 +530,6 @@ __device__ __forceinline__ void tma_load_3d_pair(uint32_t dst, const CUtensorMap
       "l"(reinterpret_cast<uint64_t>(map)), "r"(cluster_bar), "r"(x), "r"(y), "r"(z)
       : "memory");
 }
-__device__ __forceinline__ void tc_commit_pair(uint32_t cluster_bar) {
-  asm volatile(
-      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-          cluster_bar)
-      : "memory");
-}
-__device__ __forceinline__ void mma_ts_pair(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
-                                            uint32_t idesc, uint32_t accum) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::2.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accum)
-      : "memory");
-}
 // Warp-wide forms: every lane executes them with uniform operands and one
 // elected lane issues the instruction.
 __device__ __forceinline__ void mma_ts_pair_elect(uint32_t d_tmem, uint32_t a_tmem,
@@ -624,9 +609,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(NG), 1)
   // each tile = 256 query rows (a pair) of one slice, heaviest causal tiles
   // first.  Every ring and buffer index continues across tiles through the
   // global key-block counter G, so the producers run ahead into the next tile
-  // while the current one finishes; the softmax warps stage the next tile's Q
-  // before writing out the current tile's O, so QK^T of the next tile overlaps
-  // that epilogue.
+  // while the current one finishes.  Each CTA's Q rows arrive by TMA in a
+  // shared-memory buffer a tile ahead; at a tile change the softmax warps copy
+  // them into TMEM (scaled, TF32-rounded), then write the finished tile's O
+  // over them, and warp 3 stores that O by TMA and frees the buffer.
   using C = PairCfg<D, BK, NKS, NVS, NG>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -1253,20 +1239,14 @@ size_t tc_scratch_floats(const FwdParams&, int) { return 0; }
 cudaError_t launch_tc(const FwdParams& p, int precision, float*, size_t, cudaStream_t s) {
   if (precision != 0) return cudaErrorInvalidValue;
   if (p.sq > 65535 * kBM) return cudaErrorInvalidValue;
-#ifndef FA_PAIR_NG
-#define FA_PAIR_NG 2
-#endif
-#ifndef FA_D128_VK
-#define FA_D128_VK 64
-#define FA_D128_NVS 3
-#endif
-  // A pair covers 256 query rows; a single 128-row tile runs on one SM.
+  // A pair covers 256 query rows; a single 128-row tile runs on one SM.  The
+  // pair kernel runs two softmax warpgroups (four measured slower: the softmax
+  // phases are bound by issue and latency, not by the number of warps).
   const bool single = p.sq <= kBM;
   if (p.d == 128)
-    return single ? launch_tf32<128, 128, FA_D128_VK, 2, FA_D128_NVS>(p, s)
-                  : launch_tf32_pair<128, 128, 2, 2, FA_PAIR_NG>(p, s);
+    return single ? launch_tf32<128, 128, 64, 2, 3>(p, s) : launch_tf32_pair<128, 128, 2, 2, 2>(p, s);
   if (p.d == 64)
-    return single ? launch_tf32<64, 128, 128, 3, 3>(p, s) : launch_tf32_pair<64, 128, 3, 3, FA_PAIR_NG>(p, s);
+    return single ? launch_tf32<64, 128, 128, 3, 3>(p, s) : launch_tf32_pair<64, 128, 3, 3, 2>(p, s);
   return cudaErrorInvalidValue;
 }
 
