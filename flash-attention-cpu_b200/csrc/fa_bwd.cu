@@ -11,6 +11,8 @@
 // Causal masking is top-left (row i sees keys j <= i), as in the forward.
 #include "fa_common.cuh"
 
+#include <atomic>
+
 namespace fa {
 namespace {
 
@@ -298,8 +300,11 @@ size_t dq_smem() {
 
 template <int D>
 cudaError_t launch_bwd_d(const BwdParams& p, cudaStream_t s) {
-  static bool attr = false;  // set once per process (same value on every device)
-  if (!attr) {
+  static std::atomic<unsigned long long> attr_set{0};  // one bit per device
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (!(attr_set.load() & bit)) {
     cudaError_t e = cudaFuncSetAttribute(bwd_dkdv_kernel<D>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)dkdv_smem<D>());
@@ -307,7 +312,7 @@ cudaError_t launch_bwd_d(const BwdParams& p, cudaStream_t s) {
       e = cudaFuncSetAttribute(bwd_dq_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                (int)dq_smem<D>());
     if (e != cudaSuccess) return e;
-    attr = true;
+    attr_set.fetch_or(bit);
   }
   for (int b0 = 0; b0 < p.bh; b0 += 65535) {
     BwdParams q = p;

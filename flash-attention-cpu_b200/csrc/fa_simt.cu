@@ -10,6 +10,8 @@
 // max, out = acc * (l > 0 ? 1/l : 0).
 #include "fa_common.cuh"
 
+#include <atomic>
+
 #include <math.h>
 
 #include <mutex>
@@ -295,11 +297,21 @@ cudaError_t launch_simt_t(const FwdParams& p, cudaStream_t s) {
   const int sk_stride = p.d | 1;
   size_t smem = sizeof(float) * ((size_t)kSimtBQ * p.d + (size_t)kSimtBK * sk_stride +
                                  (size_t)kSimtBK * p.d);
-  if (smem > 48 * 1024) {
+  // The attribute is set once per device, to the largest size this
+  // instantiation can need (d up to DCH*32), so that concurrent calls with
+  // other d never see it lowered under them.
+  static std::atomic<unsigned long long> attr_set{0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (!(attr_set.load() & bit)) {
+    const int dmax = DCH * 32;
+    const size_t smax = sizeof(float) * ((size_t)kSimtBQ * dmax + (size_t)kSimtBK * (dmax | 1) +
+                                         (size_t)kSimtBK * dmax);
     cudaError_t e = cudaFuncSetAttribute(simt_fwd<DCH>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)smem);
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smax);
     if (e != cudaSuccess) return e;
+    attr_set.fetch_or(bit);
   }
   dim3 grid((p.sq + kSimtBQ - 1) / kSimtBQ, p.bh);
   simt_fwd<DCH><<<grid, 128, smem, s>>>(p);
