@@ -104,4 +104,58 @@ FA_CPP_MULTI(flash_attention_multihead_v3)
 FA_CPP_MULTI(flash_attention_multihead)
 #undef FA_CPP_MULTI
 
+// ---- beyond the crate's API (this library's additions) ---------------------
+
+// The multihead forward that also returns each row's LSE (natural log of the
+// scaled-score row sum), as the backward needs it.  out: [batch*heads*seq_len_q*d_head],
+// lse: [batch*heads*seq_len_q].
+inline void flash_attention_multihead_lse(std::span<const float> q, std::span<const float> k,
+                                          std::span<const float> v, std::size_t batch_heads,
+                                          std::size_t seq_len_q, std::size_t seq_len_k,
+                                          std::size_t d_head, bool causal, std::span<float> out,
+                                          std::span<float> lse) {
+  const std::size_t nq = batch_heads * seq_len_q * d_head, nk = batch_heads * seq_len_k * d_head;
+  if (q.size() != nq) throw Panic("q shape mismatch");
+  if (k.size() != nk) throw Panic("k shape mismatch");
+  if (v.size() != nk) throw Panic("v shape mismatch");
+  if (out.size() != nq) throw Panic("out shape mismatch");
+  if (lse.size() != batch_heads * seq_len_q) throw Panic("lse shape mismatch");
+  detail::check(fa_flash_attention_multihead_lse(q.data(), k.data(), v.data(), batch_heads,
+                                                 seq_len_q, seq_len_k, d_head, causal ? 1 : 0,
+                                                 out.data(), lse.data()));
+}
+
+// Gradients dq, dk, dv of the forward (exact f32), from its out and lse.
+inline void flash_attention_backward(std::span<const float> q, std::span<const float> k,
+                                     std::span<const float> v, std::span<const float> out,
+                                     std::span<const float> lse, std::span<const float> dout,
+                                     std::size_t batch_heads, std::size_t seq_len_q,
+                                     std::size_t seq_len_k, std::size_t d_head, bool causal,
+                                     std::span<float> dq, std::span<float> dk,
+                                     std::span<float> dv) {
+  const std::size_t nq = batch_heads * seq_len_q * d_head, nk = batch_heads * seq_len_k * d_head;
+  if (q.size() != nq || out.size() != nq || dout.size() != nq || dq.size() != nq)
+    throw Panic("q/out/dout/dq shape mismatch");
+  if (k.size() != nk || v.size() != nk || dk.size() != nk || dv.size() != nk)
+    throw Panic("k/v/dk/dv shape mismatch");
+  if (lse.size() != batch_heads * seq_len_q) throw Panic("lse shape mismatch");
+  detail::check(fa_flash_attention_backward(q.data(), k.data(), v.data(), out.data(), lse.data(),
+                                            dout.data(), dq.data(), dk.data(), dv.data(),
+                                            batch_heads, seq_len_q, seq_len_k, d_head,
+                                            causal ? 1 : 0));
+}
+
+// Pins a host buffer for the lifetime of the object (fa_pin_host), so host-slice
+// calls on it copy at the full PCIe rate.
+class PinnedRange {
+ public:
+  explicit PinnedRange(std::span<float> s) : p_(s.data()) { detail::check(fa_pin_host(p_, s.size_bytes())); }
+  ~PinnedRange() { fa_unpin_host(p_); }
+  PinnedRange(const PinnedRange&) = delete;
+  PinnedRange& operator=(const PinnedRange&) = delete;
+
+ private:
+  void* p_;
+};
+
 }  // namespace flash_attention_cpu

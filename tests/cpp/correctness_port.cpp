@@ -193,6 +193,35 @@ static void gpu_cases() {
     }
   }
   for (bool causal : {false, true}) run_case(23, 29, 16, 0, 0, causal);  // zero_block_size_is_clamped
+  {  // this library's additions: LSE, backward, pinned buffers (known answers)
+    // One key: P = 1, so out = v, lse = scale*q.k, dv = dout, dq = dk = 0.
+    const size_t d = 16;
+    Vec q = random_vec(d, 40), k = random_vec(d, 41), v = random_vec(d, 42), dout = random_vec(d, 43);
+    Vec out(d), lse(1), dq(d), dk(d), dv(d);
+    const int old = fa_get_precision();
+    fa_set_precision(FA_PREC_FP32);
+    flash_attention_multihead_lse(q, k, v, 1, 1, 1, d, false, out, lse);
+    float dot = 0.f;
+    for (size_t i = 0; i < d; i++) dot += q[i] * k[i];
+    CHECK(max_abs_diff(out.data(), v.data(), d) < 1e-6f, "one-key out");
+    CHECK(std::fabs(lse[0] - dot / std::sqrt(16.0f)) < 1e-5f, "one-key lse %g", lse[0]);
+    flash_attention_backward(q, k, v, out, lse, dout, 1, 1, 1, d, false, dq, dk, dv);
+    Vec zero(d, 0.f);
+    CHECK(max_abs_diff(dv.data(), dout.data(), d) < 1e-6f, "one-key dv");
+    CHECK(max_abs_diff(dq.data(), zero.data(), d) < 1e-6f, "one-key dq");
+    CHECK(max_abs_diff(dk.data(), zero.data(), d) < 1e-6f, "one-key dk");
+    fa_set_precision(old);
+    // pinned buffers give what pageable ones give
+    const size_t bh = 4, s = 300, dd = 64;
+    Vec a = random_vec(bh * s * dd, 50), b = random_vec(bh * s * dd, 51), c = random_vec(bh * s * dd, 52);
+    Vec o1(bh * s * dd), o2(bh * s * dd);
+    flash_attention_multihead_v2(a, b, c, 1, bh, s, s, dd, FlashAttentionConfig{64, 128, true}, o1);
+    {
+      PinnedRange pa(a), pb(b), pc(c), po(o2);
+      flash_attention_multihead_v2(a, b, c, 1, bh, s, s, dd, FlashAttentionConfig{64, 128, true}, o2);
+    }
+    CHECK(max_abs_diff(o1.data(), o2.data(), o1.size()) == 0.f, "pinned vs pageable");
+  }
 }
 
 int main(int argc, char** argv) {
