@@ -2,7 +2,7 @@
 
 The reference has no golden vectors; its tests pin behaviour by known answers
 and by agreement with its naive oracle.  Each test below restates one of those
-checks against the oracle, so the oracle is trusted before it judges the GPU.
+checks against the oracle, so the oracle is trusted before it checks the GPU.
 """
 import math
 
