@@ -125,7 +125,7 @@ int dispatch(fa::FwdParams p, int dev, cudaStream_t s) {
   if (p.sq <= 16 && fa::decode_supported(p.d)) {
     // Few query rows: split the key range so every SM streams K/V.
     t_path = "decode_splitkv";
-    const int splits = fa::decode_pick_splits(p.bh, p.sq, p.sk, st.num_sms);
+    const int splits = fa::decode_pick_splits(p.bh, p.sq, p.sk, st.num_sms, p.d);
     float* scratch = nullptr;
     if (splits > 1) {
       size_t n = (size_t)splits * p.bh * p.sq * (p.d + 1);
@@ -648,7 +648,7 @@ int fa_forward_decode_noalloc(const float* q, const float* k, const float* v, fl
     return set_err(FA_ERR_NO_DEVICE, std::string("no usable CUDA device: ") + cudaGetErrorString(e));
   }
   if (major != 10) return set_err(FA_ERR_NO_DEVICE, "this library is built for sm_100a (B200) only");
-  const int splits = fa::decode_pick_splits((int)bh, (int)sq, (int)sk, sms);
+  const int splits = fa::decode_pick_splits((int)bh, (int)sq, (int)sk, sms, (int)d);
   const size_t need = splits > 1 ? (size_t)splits * bh * sq * (d + 1) : 0;
   if (need > fa::static_scratch_floats())
     return set_err(FA_ERR_UNSUPPORTED,

@@ -82,7 +82,7 @@ namespace fa {
 cudaError_t launch_simt(const FwdParams& p, cudaStream_t s);
 // Split-KV decode family: partial buffers are caller-provided scratch of
 // `splits * bh * sq * (d + 1)` floats (ignored when splits == 1).
-int decode_pick_splits(int bh, int sq, int sk, int num_sms);
+int decode_pick_splits(int bh, int sq, int sk, int num_sms, int d);
 cudaError_t launch_decode(const FwdParams& p, int splits, float* scratch, cudaStream_t s);
 cudaError_t launch_combine(const float* o_parts, const float* lse_parts, int n_parts,
                            long long rows, int d, float* out, float* lse_out,

@@ -338,10 +338,32 @@ cudaError_t launch_simt(const FwdParams& p, cudaStream_t s) {
 
 bool decode_supported(int d) { return d > 0 && d % 4 == 0 && d <= 256; }
 
-int decode_pick_splits(int bh, int sq, int sk, int num_sms) {
+// 256-thread decode CTAs resident per SM on the current device (cached per
+// device and instantiation).
+static int decode_resident_per_sm(int d) {
+  static std::atomic<int> cache[64][2] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 8;
+  const int nv = d <= 128 ? 0 : 1;
+  int r = cache[dev][nv].load();
+  if (r > 0) return r;
+  const size_t smem = sizeof(float) * kDecWarps * (nv ? 256 : 128);
+  cudaError_t e = nv ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(&r, decode_fwd<2>, 256, smem)
+                     : cudaOccupancyMaxActiveBlocksPerMultiprocessor(&r, decode_fwd<1>, 256, smem);
+  if (e != cudaSuccess || r < 1) {
+    cudaGetLastError();
+    return 8;
+  }
+  cache[dev][nv].store(r);
+  return r;
+}
+
+int decode_pick_splits(int bh, int sq, int sk, int num_sms, int d) {
   const long long ctas = (long long)bh * sq;
-  const long long target = 8LL * num_sms;  // ~8 resident 256-thread CTAs per SM
-  long long splits = (target + ctas - 1) / ctas;
+  // As many splits as keep every CTA in the first (only) wave: a second wave
+  // of a few CTAs would run alone for a whole CTA's time.
+  const long long slots = (long long)decode_resident_per_sm(d) * num_sms;
+  long long splits = ctas >= slots ? 1 : slots / ctas;
   long long max_splits = (sk + 127) / 128;  // at least 128 keys per split
   if (splits > max_splits) splits = max_splits;
   if (splits < 1) splits = 1;
