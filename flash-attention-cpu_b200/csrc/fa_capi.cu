@@ -159,7 +159,15 @@ int dispatch(fa::FwdParams p, int dev, cudaStream_t s) {
   }
   if (fa::tc_supported(p.d, prec)) {
     t_path = prec == FA_PREC_TF32 ? "tcgen05_tf32" : "tcgen05_3xtf32";
-    e = fa::launch_tc(p, prec, nullptr, 0, s);
+    // a launch with few 256-row tiles splits the key range (partials + LSE merge)
+    const size_t nws = fa::tc_scratch_floats(p, st.num_sms);
+    float* ws = nullptr;
+    if (nws) {
+      e = cudaMallocAsync((void**)&ws, nws * sizeof(float), s);
+      if (e != cudaSuccess) return cuda_err(e, "cudaMallocAsync(split partials)");
+    }
+    e = fa::launch_tc(p, prec, ws, nws, s);
+    if (ws) cudaFreeAsync(ws, s);
     if (e != cudaSuccess) return cuda_err(e, "tcgen05 launch");
     return FA_OK;
   }

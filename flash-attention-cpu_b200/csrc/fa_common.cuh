@@ -70,7 +70,7 @@ __device__ __forceinline__ float warp_sum(float x) {
 
 // Visible-key count for query global position qg against keys starting at
 // global position kg0 with n keys: keys [kg0, kg0+n) ∩ (-inf, qg].
-__device__ __forceinline__ int causal_limit(long long qg, long long kg0, int n) {
+__host__ __device__ __forceinline__ int causal_limit(long long qg, long long kg0, int n) {
   long long lim = qg - kg0 + 1;
   return lim < 0 ? 0 : (lim > n ? n : (int)lim);
 }
@@ -95,7 +95,8 @@ cudaError_t static_scratch_ptr(float** out);
 bool tc_supported(int d, int precision);
 cudaError_t launch_tc(const FwdParams& p, int precision, float* scratch,
                       size_t scratch_floats, cudaStream_t s);
-size_t tc_scratch_floats(const FwdParams& p, int precision);
+// Workspace (floats) for the key-range split of small launches; 0 = no split.
+size_t tc_scratch_floats(const FwdParams& p, int num_sms);
 // 3xTF32 family (d = 64, 128): workspace of tc3_workspace_floats() floats
 // (hi/lo planes of K and V).
 size_t tc3_workspace_floats(const FwdParams& p);

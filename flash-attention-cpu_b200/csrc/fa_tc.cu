@@ -604,7 +604,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(NG), 1)
     tc_fwd_tf32_pair(const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV,
                      const __grid_constant__ CUtensorMap tmQ,
-                     const __grid_constant__ CUtensorMap tmO, FwdParams p, int n_pairs) {
+                     const __grid_constant__ CUtensorMap tmO, FwdParams p, int n_pairs,
+                     int n_split, float* split_lse) {
   // Persistent: cluster c computes work tiles w = c, c + C, ... (C clusters),
   // each tile = 256 query rows (a pair) of one slice, heaviest causal tiles
   // first.  Every ring and buffer index continues across tiles through the
@@ -659,9 +660,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(NG), 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int cid = (int)(blockIdx.x >> 1), n_clusters = (int)(gridDim.x >> 1);
-  const int n_work = n_pairs * p.bh;
+  // With n_split > 1 each tile's key blocks are divided over n_split work
+  // units, each writing its range-normalised O (through tmO, which then maps a
+  // [n_split * bh, sq, d] workspace) and LSE (split_lse) for the LSE combine.
+  const int n_work = n_pairs * p.bh * n_split;
   struct Tile {
-    int bh, q0_pair, q0, q_rows, n_kv;
+    int bh, q0_pair, q0, q_rows, j0, n_kv, z;  // z: slice index in tmO's space
   };
   // Round k of the static schedule: tiles k*C .. k*C+C-1 (heaviest first),
   // dealt in snake order (reversed on odd rounds) so that every cluster's
@@ -669,6 +673,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(NG), 1)
   auto work_of = [&](int k) { return k * n_clusters + ((k & 1) ? n_clusters - 1 - cid : cid); };
   auto tile_of = [&](int w) {
     Tile t;
+    const int sp = w % n_split;
+    w /= n_split;
     const int pair = n_pairs - 1 - w / p.bh;  // heaviest causal pairs first
     t.bh = w % p.bh;
     t.q0_pair = pair * 2 * kBM;
@@ -677,7 +683,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(NG), 1)
     const int pair_rows = min(2 * kBM, p.sq - t.q0_pair);
     int kend = p.sk;
     if (p.causal) kend = causal_limit(p.q_offset + t.q0_pair + pair_rows - 1, p.k_offset, p.sk);
-    t.n_kv = (kend + BK - 1) / BK;
+    const int nb = (kend + BK - 1) / BK;
+    t.j0 = (int)((long long)sp * nb / n_split);
+    t.n_kv = (int)((long long)(sp + 1) * nb / n_split) - t.j0;
+    t.z = sp * p.bh + t.bh;
     return t;
   };
 
@@ -756,12 +765,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(NG), 1)
             mbar_expect_tx_cluster(full, C::kKBytes);
             for (int c = 0; c < D / 32; c++)
               tma_load_3d_pair(sK + s * C::kKBytes + c * C::kKHalf * 128, &tmK, full, 32 * c,
-                               j * BK + (int)rank * C::kKHalf, t.bh);
+                               (t.j0 + j) * BK + (int)rank * C::kKHalf, t.bh);
           } else {
             mbar_expect_tx_cluster(full, C::kVBytes);
             for (int c = 0; c < C::kDHalf / 32; c++)
               tma_load_3d_pair(sV + s * C::kVBytes + c * BK * 128, &tmV, full,
-                               (int)rank * C::kDHalf + 32 * c, j * BK, t.bh);
+                               (int)rank * C::kDHalf + 32 * c, (t.j0 + j) * BK, t.bh);
           }
         }
       }
@@ -855,7 +864,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(NG), 1)
       auto store = [&](bool last) {
         if (pt.q_rows > 0)
           for (int c = 0; c < D / 32; c++)
-            tma_store_3d(&tmO, sQ + c * (kBM * 128), 32 * c, pt.q0, pt.bh);
+            tma_store_3d(&tmO, sQ + c * (kBM * 128), 32 * c, pt.q0, pt.z);
         bulk_commit();
         if (last)
           bulk_wait_all();
@@ -1002,8 +1011,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(NG), 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(bar_o_smem_full);
       }
-      if (ok && have_prev && g == 0 && r < pt.q_rows && p.lse)
-        p.lse[(size_t)pt.bh * p.sq + pt.q0 + r] =
+      if (ok && have_prev && g == 0 && r < pt.q_rows && (p.lse || split_lse))
+        (split_lse ? split_lse + (size_t)pt.z * p.sq : p.lse + (size_t)pt.bh * p.sq)[pt.q0 + r] =
             l_prev > 0.0f ? (pm + __log2f(l_prev)) * 0.69314718055994530942f : -INFINITY;
       float m = -INFINITY, l = 0.0f;  // l: this half's partial row sum
       for (int j = 0; j < t.n_kv && ok; j++) {
@@ -1026,7 +1035,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(NG), 1)
 #pragma unroll
           for (int e = 0; e < HC; e++) x[e] = -INFINITY;
         }
-        const int kbase = j * BK + g * HC;
+        const int kbase = (t.j0 + j) * BK + g * HC;
         int lim = min(HC, p.sk - kbase);
         if (p.causal) lim = min(lim, causal_limit(qg, p.k_offset + kbase, HC));
         if (!__all_sync(0xffffffffu, lim == HC)) {
@@ -1131,8 +1140,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(NG), 1)
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(bar_o_smem_full);
-        if (g == 0 && r < pt.q_rows && p.lse)
-          p.lse[(size_t)pt.bh * p.sq + pt.q0 + r] =
+        if (g == 0 && r < pt.q_rows && (p.lse || split_lse))
+          (split_lse ? split_lse + (size_t)pt.z * p.sq : p.lse + (size_t)pt.bh * p.sq)[pt.q0 + r] =
               l_prev > 0.0f ? (pm + __log2f(l_prev)) * 0.69314718055994530942f : -INFINITY;
       }
     }
@@ -1180,15 +1189,21 @@ cudaError_t launch_tf32(const FwdParams& p, cudaStream_t s) {
   return cudaGetLastError();
 }
 
+// n_split > 1: partials go to ws ([n_split][bh][sq][d] then [n_split][bh][sq])
+// and are merged into p.o / p.lse by the LSE combine kernel.
 template <int D, int BK, int NKS, int NVS, int NG>
-cudaError_t launch_tf32_pair(const FwdParams& p, cudaStream_t s) {
+cudaError_t launch_tf32_pair(const FwdParams& p, cudaStream_t s, int n_split = 1,
+                             float* ws = nullptr) {
   using C = PairCfg<D, BK, NKS, NVS, NG>;
   CUtensorMap mk, mv;
   CUtensorMap mq, mo;
+  const long long rows = (long long)p.bh * p.sq;
+  float* ws_lse = n_split > 1 ? ws + (size_t)n_split * rows * D : nullptr;
   if (!make_map(&mk, p.k, D, p.sk, p.bh, BK / 2, CU_TENSOR_MAP_SWIZZLE_128B) ||
       !make_map(&mv, p.v, D, p.sk, p.bh, BK, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B) ||
       !make_map(&mq, p.q, D, p.sq, p.bh, kBM, CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !make_map(&mo, p.o, D, p.sq, p.bh, kBM, CU_TENSOR_MAP_SWIZZLE_128B))
+      !make_map(&mo, n_split > 1 ? ws : p.o, D, p.sq, p.bh * n_split, kBM,
+                CU_TENSOR_MAP_SWIZZLE_128B))
     return cudaErrorInvalidValue;
   static std::atomic<unsigned long long> attr_set{0};  // one bit per device
   static int sm_count[64] = {};
@@ -1205,14 +1220,16 @@ cudaError_t launch_tf32_pair(const FwdParams& p, cudaStream_t s) {
     attr_set.fetch_or(bit);
   }
   const int n_pairs = (p.sq + 2 * kBM - 1) / (2 * kBM);
-  const long long n_work = (long long)n_pairs * p.bh;
+  const long long n_work = (long long)n_pairs * p.bh * n_split;
   // persistent: one cluster (2 SMs) per SM pair, at most one per work tile
   const int n_clusters = (int)(n_work < sm_count[dev & 63] / 2 ? n_work : sm_count[dev & 63] / 2);
   if (n_work > INT32_MAX) return cudaErrorInvalidValue;
   tc_fwd_tf32_pair<D, BK, NKS, NVS, NG><<<dim3(2 * n_clusters), pair_threads(NG), C::kSmemBytes, s>>>(
-      mk, mv, mq, mo, p, n_pairs);
+      mk, mv, mq, mo, p, n_pairs, n_split, ws_lse);
   count_launch();
-  return cudaGetLastError();
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess || n_split == 1) return e;
+  return launch_combine(ws, ws_lse, n_split, rows, D, p.o, p.lse, s);
 }
 
 }  // namespace
@@ -1234,19 +1251,55 @@ bool tc_supported(int d, int precision) {
   return precision == 0 && (d == 64 || d == 128);
 }
 
-size_t tc_scratch_floats(const FwdParams&, int) { return 0; }
+// Key-range splits for the pair kernel: when the work tiles (256 rows of one
+// slice) are at most half the SM pairs, each tile's key blocks are divided so
+// that the units fill the pairs in one round, as long as the heaviest unit keeps
+// enough blocks (8 at d = 128, 16 at d = 64) to outweigh the partials' extra
+// traffic and the merge launch; at most 16 units per tile.  Measured on one
+// B200: one 4096-row head 54 -> 35 us (4 units), one 8192-row causal head
+// 98 -> 72 us (2 units); shorter slices (1 x 512, 4 x 2048 at d 64) got slower
+// and are left whole.
+int tc_pick_splits(const FwdParams& p, int num_sms) {
+  if (p.sq <= kBM || !(p.d == 64 || p.d == 128)) return 1;
+  const long long n_pairs = (p.sq + 2 * kBM - 1) / (2 * kBM);
+  const long long n_work = n_pairs * p.bh;
+  const long long clusters = num_sms / 2;
+  if (n_work * 2 > clusters) return 1;
+  int kend = p.sk;
+  if (p.causal) kend = causal_limit(p.q_offset + p.sq - 1, p.k_offset, p.sk);
+  const long long max_nkv = (kend + 127) / 128;
+  const long long min_blocks = p.d == 128 ? 8 : 16;
+  long long split = clusters / n_work;
+  if (split > max_nkv / min_blocks) split = max_nkv / min_blocks;
+  if (split > 16) split = 16;
+  return split < 1 ? 1 : (int)split;
+}
 
-cudaError_t launch_tc(const FwdParams& p, int precision, float*, size_t, cudaStream_t s) {
+size_t tc_scratch_floats(const FwdParams& p, int num_sms) {
+  const int split = tc_pick_splits(p, num_sms);
+  return split > 1 ? (size_t)split * p.bh * p.sq * (p.d + 1) : 0;
+}
+
+cudaError_t launch_tc(const FwdParams& p, int precision, float* scratch, size_t scratch_floats,
+                      cudaStream_t s) {
   if (precision != 0) return cudaErrorInvalidValue;
   if (p.sq > 65535 * kBM) return cudaErrorInvalidValue;
+  // split the key ranges when the scratch for it was provided
+  int split = 1;
+  if (scratch && scratch_floats > 0) {
+    split = (int)(scratch_floats / ((size_t)p.bh * p.sq * (p.d + 1)));
+    if (split < 1) split = 1;
+  }
   // A pair covers 256 query rows; a single 128-row tile runs on one SM.  The
   // pair kernel runs two softmax warpgroups (four measured slower: the softmax
   // phases are bound by issue and latency, not by the number of warps).
   const bool single = p.sq <= kBM;
   if (p.d == 128)
-    return single ? launch_tf32<128, 128, 64, 2, 3>(p, s) : launch_tf32_pair<128, 128, 2, 2, 2>(p, s);
+    return single ? launch_tf32<128, 128, 64, 2, 3>(p, s)
+                  : launch_tf32_pair<128, 128, 2, 2, 2>(p, s, split, scratch);
   if (p.d == 64)
-    return single ? launch_tf32<64, 128, 128, 3, 3>(p, s) : launch_tf32_pair<64, 128, 3, 3, 2>(p, s);
+    return single ? launch_tf32<64, 128, 128, 3, 3>(p, s)
+                  : launch_tf32_pair<64, 128, 3, 3, 2>(p, s, split, scratch);
   return cudaErrorInvalidValue;
 }
 

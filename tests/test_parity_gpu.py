@@ -352,8 +352,10 @@ def test_pageable_host_buffers_go_through_pinned_staging(fa, prec):
     dlse = torch.empty(bh, s, device="cuda")
     fa.forward_device(dq, dk, dv, dout, dlse, causal=True)
     fa.sync_status()
-    assert np.array_equal(out, dout.cpu().numpy().ravel())
-    assert np.array_equal(lse, dlse.cpu().numpy().ravel())
+    # (the staged call runs in chunks of slices, whose launches may split key
+    # ranges differently from one launch over all slices: equal to rounding)
+    assert max_abs_diff(out, dout.cpu().numpy().ravel()) < 1e-5
+    assert max_abs_diff(lse, dlse.cpu().numpy().ravel()) < 1e-5
     out2 = np.zeros(bh * s * d, np.float32)
     fa.flash_attention_multihead_v2(q, k, v, 1, bh, s, s, d, fa.FlashAttentionConfig(64, 128, True),
                                     out2)
@@ -379,4 +381,21 @@ def test_pinned_host_buffers_via_fa_pin_host(fa):
     finally:
         for a in (q, k, v, out):
             fa.unpin_host(a)
-    assert np.array_equal(out, staged)
+    assert max_abs_diff(out, staged) < 1e-5
+
+
+@pytest.mark.parametrize("shape", [(1, 4096, 4096, 128, True), (1, 4096, 4096, 128, False),
+                                   (1, 512, 512, 64, False), (2, 1000, 3000, 128, True),
+                                   (3, 700, 700, 64, True)])
+def test_key_range_split_of_small_launches(fa, shape):
+    # Few 256-row tiles: the pair kernel divides each tile's key blocks over
+    # several work units and merges their partials by LSE.
+    bh, sq, sk, d, causal = shape
+    fa.set_precision(fa.PREC_TF32)
+    q, k, v = (random_vec(bh * sq * d, 91), random_vec(bh * sk * d, 92),
+               random_vec(bh * sk * d, 93))
+    out, lse = fa.multihead_lse(q, k, v, bh, sq, sk, d, causal)
+    assert fa.last_path() == "tcgen05_tf32"
+    want, wlse, _ = O.flash_v2_multihead(q, k, v, bh, sq, sk, d, causal)
+    assert max_abs_diff(out, want) < 2e-3
+    assert max_abs_diff(lse, wlse) < 2e-3
