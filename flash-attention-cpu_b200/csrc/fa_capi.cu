@@ -150,9 +150,9 @@ int dispatch(fa::FwdParams p, int dev, cudaStream_t s) {
   if (prec == FA_PREC_3XTF32 && (p.d == 64 || p.d == 128)) {
     t_path = "tcgen05_3xtf32";
     float* ws = nullptr;
-    e = cudaMallocAsync((void**)&ws, fa::tc3_workspace_floats(p) * sizeof(float), s);
+    e = cudaMallocAsync((void**)&ws, fa::tc3_workspace_floats(p, st.num_sms) * sizeof(float), s);
     if (e != cudaSuccess) return cuda_err(e, "cudaMallocAsync(3xTF32 split planes)");
-    e = fa::launch_tc3(p, ws, s);
+    e = fa::launch_tc3(p, ws, st.num_sms, s);
     cudaFreeAsync(ws, s);
     if (e != cudaSuccess) return cuda_err(e, "tcgen05 3xTF32 launch");
     return FA_OK;

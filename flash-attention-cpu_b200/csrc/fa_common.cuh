@@ -98,9 +98,9 @@ cudaError_t launch_tc(const FwdParams& p, int precision, float* scratch,
 // Workspace (floats) for the key-range split of small launches; 0 = no split.
 size_t tc_scratch_floats(const FwdParams& p, int num_sms);
 // 3xTF32 family (d = 64, 128): workspace of tc3_workspace_floats() floats
-// (hi/lo planes of K and V).
-size_t tc3_workspace_floats(const FwdParams& p);
-cudaError_t launch_tc3(const FwdParams& p, float* ws, cudaStream_t s);
+// (hi/lo planes of K and V, then the key-range partials of small launches).
+size_t tc3_workspace_floats(const FwdParams& p, int num_sms);
+cudaError_t launch_tc3(const FwdParams& p, float* ws, int num_sms, cudaStream_t s);
 unsigned long long launches_issued();
 void count_launch(int n = 1);
 

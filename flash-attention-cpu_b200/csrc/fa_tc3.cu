@@ -68,7 +68,7 @@ template <int D, int BK, int NKS, int NVS, int NSB>
 __global__ void __launch_bounds__(kThreads, 1)
     tc_fwd_3xtf32(const __grid_constant__ CUtensorMap tmKh, const __grid_constant__ CUtensorMap tmKl,
                   const __grid_constant__ CUtensorMap tmVh, const __grid_constant__ CUtensorMap tmVl,
-                  FwdParams p) {
+                  FwdParams p, float* split_o, float* split_lse) {
   using C = Tc3Cfg<D, BK, NKS, NVS, NSB>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -98,7 +98,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int q_rows = min(kBM, p.sq - q0);
   int kend = p.sk;
   if (p.causal) kend = causal_limit(p.q_offset + q0 + q_rows - 1, p.k_offset, p.sk);
-  const int n_kv = (kend + BK - 1) / BK;
+  // blockIdx.z: the part of the key range this CTA covers (gridDim.z parts);
+  // with more than one part the range-normalised O and LSE go to split_o /
+  // split_lse ([part][bh][sq]) for the LSE combine.
+  const int nb = (kend + BK - 1) / BK;
+  const int j0 = (int)((long long)blockIdx.z * nb / gridDim.z);
+  const int n_kv = (int)((long long)(blockIdx.z + 1) * nb / gridDim.z) - j0;
+  const bool to_split = gridDim.z > 1;
+  const size_t zrow = (size_t)(blockIdx.z * gridDim.x + bh) * p.sq;  // row base in split space
 
   if (threadIdx.x == 0) {
     mbar_init(bar_q_full, 128);
@@ -154,9 +161,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_expect_tx(full, 2 * C::kKBytes);
         const uint32_t base = (is_k ? sK : sV) + s * 2 * C::kKBytes;
         for (int c = 0; c < C::kChunks; c++) {
-          tma_load_3d(base + c * BK * 128, is_k ? &tmKh : &tmVh, full, 32 * c, j * BK, bh);
+          tma_load_3d(base + c * BK * 128, is_k ? &tmKh : &tmVh, full, 32 * c, (j0 + j) * BK, bh);
           tma_load_3d(base + C::kKBytes + c * BK * 128, is_k ? &tmKl : &tmVl, full, 32 * c,
-                      j * BK, bh);
+                      (j0 + j) * BK, bh);
         }
         issued = j + 1;
       }
@@ -270,7 +277,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int e = 0; e < BK; e++) x[e] = __uint_as_float(sr[e]);
       }
-      const int kbase = j * BK;
+      const int kbase = (j0 + j) * BK;
       int lim = min(BK, p.sk - kbase);
       if (p.causal) lim = min(lim, causal_limit(qg, p.k_offset + kbase, BK));
       if (!__all_sync(0xffffffffu, lim == BK)) {
@@ -342,7 +349,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const float inv_l = l > 0.0f ? 1.0f / l : 0.0f;
       const bool row_ok = r < q_rows;
-      float* orow = p.o + ((size_t)bh * p.sq + q0 + r) * D;
+      float* orow = to_split ? split_o + (zrow + q0 + r) * D : p.o + ((size_t)bh * p.sq + q0 + r) * D;
 #pragma unroll
       for (int c = 0; c < D / 32; c++) {
         uint32_t rr[32];
@@ -363,8 +370,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      if (row_ok && p.lse)
-        p.lse[(size_t)bh * p.sq + q0 + r] =
+      if (row_ok && (to_split || p.lse))
+        (to_split ? split_lse + zrow : p.lse + (size_t)bh * p.sq)[q0 + r] =
             l > 0.0f ? (m + log2f(l)) * 0.69314718055994530942f : -INFINITY;
     }
     tc_fence_before();
@@ -379,7 +386,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 template <int D, int BK, int NKS, int NVS, int NSB>
-cudaError_t launch_3x(const FwdParams& p, float* ws, cudaStream_t s) {
+cudaError_t launch_3x(const FwdParams& p, float* ws, int n_split, cudaStream_t s) {
   using C = Tc3Cfg<D, BK, NKS, NVS, NSB>;
   const size_t n = (size_t)p.bh * p.sk * D;  // floats per K (or V) plane
   float* kh = ws;
@@ -411,20 +418,47 @@ cudaError_t launch_3x(const FwdParams& p, float* ws, cudaStream_t s) {
     if (e != cudaSuccess) return e;
     attr_set.fetch_or(bit);
   }
-  dim3 grid(p.bh, (p.sq + kBM - 1) / kBM);
-  tc_fwd_3xtf32<D, BK, NKS, NVS, NSB><<<grid, kThreads, C::kSmemBytes, s>>>(mkh, mkl, mvh, mvl, p);
+  const size_t rows = (size_t)p.bh * p.sq;
+  float* split_o = n_split > 1 ? ws + 4 * n : nullptr;
+  float* split_lse = n_split > 1 ? split_o + (size_t)n_split * rows * D : nullptr;
+  dim3 grid(p.bh, (p.sq + kBM - 1) / kBM, n_split);
+  tc_fwd_3xtf32<D, BK, NKS, NVS, NSB><<<grid, kThreads, C::kSmemBytes, s>>>(mkh, mkl, mvh, mvl, p,
+                                                                            split_o, split_lse);
   count_launch();
-  return cudaGetLastError();
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess || n_split == 1) return e;
+  return launch_combine(split_o, split_lse, n_split, (long long)rows, D, p.o, p.lse, s);
 }
 
 }  // namespace
 
-size_t tc3_workspace_floats(const FwdParams& p) { return 4 * (size_t)p.bh * p.sk * p.d; }
+// Key-range parts per CTA tile: with fewer CTAs (one per 128-row tile) than
+// half the SMs, each tile's key blocks are divided over up to 16 CTAs so that
+// the launch fills the SMs, while every part keeps at least 8 blocks of 64 keys.
+static int tc3_pick_splits(const FwdParams& p, int num_sms) {
+  const long long ctas = (long long)p.bh * ((p.sq + kBM - 1) / kBM);
+  if (ctas * 2 > num_sms) return 1;
+  int kend = p.sk;
+  if (p.causal) kend = causal_limit(p.q_offset + p.sq - 1, p.k_offset, p.sk);
+  const long long nb = (kend + 63) / 64;
+  long long split = num_sms / ctas;
+  if (split > nb / 8) split = nb / 8;
+  if (split > 16) split = 16;
+  return split < 1 ? 1 : (int)split;
+}
 
-cudaError_t launch_tc3(const FwdParams& p, float* ws, cudaStream_t s) {
+size_t tc3_workspace_floats(const FwdParams& p, int num_sms) {
+  const int split = tc3_pick_splits(p, num_sms);
+  size_t f = 4 * (size_t)p.bh * p.sk * p.d;  // hi / lo planes of K and V
+  if (split > 1) f += (size_t)split * p.bh * p.sq * (p.d + 1);
+  return f;
+}
+
+cudaError_t launch_tc3(const FwdParams& p, float* ws, int num_sms, cudaStream_t s) {
   if (p.sq > 65535 * kBM) return cudaErrorInvalidValue;
-  if (p.d == 128) return launch_3x<128, 64, 2, 1, 1>(p, ws, s);
-  if (p.d == 64) return launch_3x<64, 64, 3, 3, 2>(p, ws, s);
+  const int split = tc3_pick_splits(p, num_sms);
+  if (p.d == 128) return launch_3x<128, 64, 2, 1, 1>(p, ws, split, s);
+  if (p.d == 64) return launch_3x<64, 64, 3, 3, 2>(p, ws, split, s);
   return cudaErrorInvalidValue;
 }
 

@@ -384,18 +384,19 @@ def test_pinned_host_buffers_via_fa_pin_host(fa):
     assert max_abs_diff(out, staged) < 1e-5
 
 
+@pytest.mark.parametrize("prec", [0, 1])
 @pytest.mark.parametrize("shape", [(1, 4096, 4096, 128, True), (1, 4096, 4096, 128, False),
                                    (1, 512, 512, 64, False), (2, 1000, 3000, 128, True),
-                                   (3, 700, 700, 64, True)])
-def test_key_range_split_of_small_launches(fa, shape):
-    # Few 256-row tiles: the pair kernel divides each tile's key blocks over
-    # several work units and merges their partials by LSE.
+                                   (3, 700, 700, 64, True), (1, 2048, 2048, 64, False)])
+def test_key_range_split_of_small_launches(fa, prec, shape):
+    # Few tiles: the tcgen05 kernels divide each tile's key blocks over several
+    # work units (TF32) or CTAs (3xTF32) and merge their partials by LSE.
     bh, sq, sk, d, causal = shape
-    fa.set_precision(fa.PREC_TF32)
+    fa.set_precision(prec)
     q, k, v = (random_vec(bh * sq * d, 91), random_vec(bh * sk * d, 92),
                random_vec(bh * sk * d, 93))
     out, lse = fa.multihead_lse(q, k, v, bh, sq, sk, d, causal)
-    assert fa.last_path() == "tcgen05_tf32"
+    assert fa.last_path() == ("tcgen05_tf32" if prec == 0 else "tcgen05_3xtf32")
     want, wlse, _ = O.flash_v2_multihead(q, k, v, bh, sq, sk, d, causal)
-    assert max_abs_diff(out, want) < 2e-3
-    assert max_abs_diff(lse, wlse) < 2e-3
+    assert max_abs_diff(out, want) < TOL[prec]
+    assert max_abs_diff(lse, wlse) < TOL[prec]
