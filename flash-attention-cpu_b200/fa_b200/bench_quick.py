@@ -3,7 +3,8 @@
 The counterpart of the crate's ``examples/bench_quick.rs``: the same shapes
 ((256, 64), (512, 64), (1024, 64), (2048, 64), (1024, 128)), the same
 variants (v1, v2, v3, non-causal and causal, through the host-slice calls),
-one untimed warm-up call and then the mean over a few calls.  On the GPU the
+one untimed warm-up call, then the median over 20-30 calls (the crate takes
+the mean of 3-10 calls; GPU calls this short need more to be stable).  On the GPU the
 three variants run the same kernels, so their rows differ only by noise; the
 ``device`` variant times the same work through ``fa_forward_device`` on
 resident tensors (no PCIe), which is what the kernels alone cost.  The crate's
@@ -56,14 +57,20 @@ def random_vec(n: int, seed: int):
 
 
 def time_it(fn, iters: int) -> float:
+    """Median seconds per call over `iters` timed calls after one warm-up call.
+    (The median, since single calls of a few hundred microseconds see
+    scheduling noise that a mean over a handful of calls would keep.)"""
     fn()  # warm-up (first-touch, caches) outside the timed loop
-    t0 = time.perf_counter()
+    ts = []
     for _ in range(iters):
+        t0 = time.perf_counter()
         fn()
-    return (time.perf_counter() - t0) / iters
+        ts.append(time.perf_counter() - t0)
+    ts.sort()
+    return ts[len(ts) // 2]
 
 
-def measure(fa, iters_small: int = 10, iters_large: int = 3):
+def measure(fa, iters_small: int = 30, iters_large: int = 20):
     """Rows (variant, causal, seq_len, d_head, time_ms) for the current precision."""
     import numpy as np
     import torch
