@@ -149,4 +149,6 @@ def main(argv=None) -> int:
 
 
 if __name__ == "__main__":
+    import signal
+    signal.signal(signal.SIGPIPE, signal.SIG_DFL)  # quiet when piped into head
     sys.exit(main())
