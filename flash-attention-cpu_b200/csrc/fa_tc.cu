@@ -102,7 +102,7 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
 template <int D, int BK, int VK, int NKS, int NVS>
 __global__ void __launch_bounds__(kThreads, 1)
     tc_fwd_tf32(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
-                FwdParams p) {
+                FwdParams p, float* split_o, float* split_lse) {
   using C = TcCfg<D, BK, VK, NKS, NVS>;
   constexpr int VS = C::kVS;
   extern __shared__ uint8_t smem_raw[];
@@ -143,7 +143,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int q_rows = min(kBM, p.sq - q0);
   int kend = p.sk;
   if (p.causal) kend = causal_limit(p.q_offset + q0 + q_rows - 1, p.k_offset, p.sk);
-  const int n_kv = (kend + BK - 1) / BK;
+  // blockIdx.z: the part of the key range this CTA covers (gridDim.z parts);
+  // with more than one part the range-normalised O and LSE go to split_o /
+  // split_lse ([part][bh][sq]) for the LSE combine.
+  const int nb = (kend + BK - 1) / BK;
+  const int j0 = (int)((long long)blockIdx.z * nb / gridDim.z);
+  const int n_kv = (int)((long long)(blockIdx.z + 1) * nb / gridDim.z) - j0;
+  const bool to_split = gridDim.z > 1;
+  const size_t zrow = (size_t)(blockIdx.z * gridDim.x + bh) * p.sq;
 
   if (threadIdx.x == 0) {
     mbar_init(bar_q_full, 128);
@@ -199,7 +206,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!ok) break;
         mbar_expect_tx(bar_k_full(sk), C::kKBytes);
         for (int c = 0; c < C::kChunks; c++)
-          tma_load_3d(sK + sk * C::kKBytes + c * BK * 128, &tmK, bar_k_full(sk), 32 * c, j * BK, bh);
+          tma_load_3d(sK + sk * C::kKBytes + c * BK * 128, &tmK, bar_k_full(sk), 32 * c,
+                      (j0 + j) * BK, bh);
         issued = j + 1;
       }
       // Wait (bounded, ignoring the abort flag) for the last load of every
@@ -226,7 +234,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!ok) break;
         mbar_expect_tx(bar_v_full(sv), C::kVBytes);
         for (int c = 0; c < C::kChunks; c++)
-          tma_load_3d(sV + sv * C::kVBytes + c * VK * 128, &tmV, bar_v_full(sv), 32 * c, g * VK, bh);
+          tma_load_3d(sV + sv * C::kVBytes + c * VK * 128, &tmV, bar_v_full(sv), 32 * c,
+                      j0 * BK + g * VK, bh);
         issued = g + 1;
       }
       volatile int no_abort = 0;
@@ -350,7 +359,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int e = 0; e < BK; e++) x[e] = __uint_as_float(sr[e]);
       }
       // visible keys of this row in tile j: [0, lim); mask only partial tiles
-      const int kbase = j * BK;
+      const int kbase = (j0 + j) * BK;
       int lim = min(BK, p.sk - kbase);
       if (p.causal) lim = min(lim, causal_limit(qg, p.k_offset + kbase, BK));
       if (!__all_sync(0xffffffffu, lim == BK)) {
@@ -437,7 +446,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const float inv_l = l > 0.0f ? 1.0f / l : 0.0f;
       const bool row_ok = r < q_rows;
-      float* orow = p.o + ((size_t)bh * p.sq + q0 + r) * D;
+      float* orow = to_split ? split_o + (zrow + q0 + r) * D : p.o + ((size_t)bh * p.sq + q0 + r) * D;
 #pragma unroll
       for (int c = 0; c < D / 32; c++) {
         uint32_t rr[32];
@@ -458,8 +467,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      if (row_ok && p.lse)
-        p.lse[(size_t)bh * p.sq + q0 + r] =
+      if (row_ok && (to_split || p.lse))
+        (to_split ? split_lse + zrow : p.lse + (size_t)bh * p.sq)[q0 + r] =
             l > 0.0f ? (m + __log2f(l)) * 0.69314718055994530942f : -INFINITY;
     }
     tc_fence_before();
@@ -1165,7 +1174,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(NG), 1)
 
 // ---- host side -------------------------------------------------------------
 template <int D, int BK, int VK, int NKS, int NVS>
-cudaError_t launch_tf32(const FwdParams& p, cudaStream_t s) {
+cudaError_t launch_tf32(const FwdParams& p, cudaStream_t s, int n_split = 1, float* ws = nullptr) {
   using C = TcCfg<D, BK, VK, NKS, NVS>;
   CUtensorMap mk, mv;
   if (!make_map(&mk, p.k, D, p.sk, p.bh, BK, CU_TENSOR_MAP_SWIZZLE_128B) ||
@@ -1183,10 +1192,14 @@ cudaError_t launch_tf32(const FwdParams& p, cudaStream_t s) {
     attr_set.fetch_or(bit);
   }
   const int n_qt = (p.sq + kBM - 1) / kBM;
-  dim3 grid(p.bh, n_qt);
-  tc_fwd_tf32<D, BK, VK, NKS, NVS><<<grid, kThreads, C::kSmemBytes, s>>>(mk, mv, p);
+  const size_t rows = (size_t)p.bh * p.sq;
+  float* split_lse = n_split > 1 ? ws + (size_t)n_split * rows * D : nullptr;
+  dim3 grid(p.bh, n_qt, n_split);
+  tc_fwd_tf32<D, BK, VK, NKS, NVS><<<grid, kThreads, C::kSmemBytes, s>>>(mk, mv, p, ws, split_lse);
   count_launch();
-  return cudaGetLastError();
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess || n_split == 1) return e;
+  return launch_combine(ws, split_lse, n_split, (long long)rows, D, p.o, p.lse, s);
 }
 
 // n_split > 1: partials go to ws ([n_split][bh][sq][d] then [n_split][bh][sq])
@@ -1258,9 +1271,28 @@ bool tc_supported(int d, int precision) {
 // traffic and the merge launch; at most 16 units per tile.  Measured on one
 // B200: one 4096-row head 54 -> 35 us (4 units), one 8192-row causal head
 // 98 -> 72 us (2 units); shorter slices (1 x 512, 4 x 2048 at d 64) got slower
-// and are left whole.
+// and are left whole.  Launches of at most 128 query rows (one CTA per slice in
+// the single-CTA kernel, e.g. a chunk of a prefill against a long cache) split
+// over blockIdx.z the same way when the slices are at most half the SMs.
 int tc_pick_splits(const FwdParams& p, int num_sms) {
-  if (p.sq <= kBM || !(p.d == 64 || p.d == 128)) return 1;
+  if (!(p.d == 64 || p.d == 128)) return 1;
+  if (p.sq <= kBM) {
+    // Single-CTA kernel, one CTA per slice.  Measured on one B200 (128 rows,
+    // d 128): the split pays up to ~20 slices on 4096 keys (51 -> 32 us), is
+    // neutral at 40 and slower at 74 (60 -> 78 us), so it needs 4 SMs per
+    // slice; parts keep 4 blocks of 128 keys on caches up to 8k keys and 8 on
+    // longer ones (1 x 100 x 32768: 320 -> 32 us with 32 parts), at most 64.
+    if ((long long)p.bh * 4 > num_sms) return 1;
+    int kend1 = p.sk;
+    if (p.causal) kend1 = causal_limit(p.q_offset + p.sq - 1, p.k_offset, p.sk);
+    const long long nb1 = (kend1 + 127) / 128;
+    if (nb1 < 16) return 1;
+    const long long min_blocks1 = nb1 >= 128 ? 8 : 4;
+    long long split1 = num_sms / p.bh;
+    if (split1 > nb1 / min_blocks1) split1 = nb1 / min_blocks1;
+    if (split1 > 64) split1 = 64;
+    return split1 < 1 ? 1 : (int)split1;
+  }
   const long long n_pairs = (p.sq + 2 * kBM - 1) / (2 * kBM);
   const long long n_work = n_pairs * p.bh;
   const long long clusters = num_sms / 2;
@@ -1295,10 +1327,10 @@ cudaError_t launch_tc(const FwdParams& p, int precision, float* scratch, size_t 
   // phases are bound by issue and latency, not by the number of warps).
   const bool single = p.sq <= kBM;
   if (p.d == 128)
-    return single ? launch_tf32<128, 128, 64, 2, 3>(p, s)
+    return single ? launch_tf32<128, 128, 64, 2, 3>(p, s, split, scratch)
                   : launch_tf32_pair<128, 128, 2, 2, 2>(p, s, split, scratch);
   if (p.d == 64)
-    return single ? launch_tf32<64, 128, 128, 3, 3>(p, s)
+    return single ? launch_tf32<64, 128, 128, 3, 3>(p, s, split, scratch)
                   : launch_tf32_pair<64, 128, 3, 3, 2>(p, s, split, scratch);
   return cudaErrorInvalidValue;
 }

@@ -387,7 +387,9 @@ def test_pinned_host_buffers_via_fa_pin_host(fa):
 @pytest.mark.parametrize("prec", [0, 1])
 @pytest.mark.parametrize("shape", [(1, 4096, 4096, 128, True), (1, 4096, 4096, 128, False),
                                    (1, 512, 512, 64, False), (2, 1000, 3000, 128, True),
-                                   (3, 700, 700, 64, True), (1, 2048, 2048, 64, False)])
+                                   (3, 700, 700, 64, True), (1, 2048, 2048, 64, False),
+                                   (1, 100, 20000, 128, False), (2, 128, 8192, 64, False),
+                                   (1, 77, 9000, 128, True), (1, 96, 32768, 128, False)])
 def test_key_range_split_of_small_launches(fa, prec, shape):
     # Few tiles: the tcgen05 kernels divide each tile's key blocks over several
     # work units (TF32) or CTAs (3xTF32) and merge their partials by LSE.
