@@ -684,8 +684,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(NG), 1)
     Tile t;
     const int sp = w % n_split;
     w /= n_split;
-    const int pair = n_pairs - 1 - w / p.bh;  // heaviest causal pairs first
-    t.bh = w % p.bh;
+    // Causal: heaviest pairs first (pair-major), for the balance of the
+    // persistent schedule.  Non-causal pairs cost the same, so they go
+    // slice-major: the pairs of one slice run at the same time and share its
+    // K/V through L2 (measured on one B200, 32 x 4096 x 128 non-causal:
+    // 416 -> 377 us).
+    int pair;
+    if (p.causal) {
+      pair = n_pairs - 1 - w / p.bh;
+      t.bh = w % p.bh;
+    } else {
+      pair = w % n_pairs;
+      t.bh = w / n_pairs;
+    }
     t.q0_pair = pair * 2 * kBM;
     t.q0 = t.q0_pair + (int)rank * kBM;
     t.q_rows = max(0, min(kBM, p.sq - t.q0));
