@@ -593,7 +593,7 @@ struct PairCfg {
   static constexpr int kOffV = NKS * kKBytes;
   static constexpr int kOffQ = kOffV + NVS * kVBytes;   // D/32 swizzled [128 x 32] chunks
   static constexpr int kOffBar = kOffQ + kQBytes;
-  static constexpr int kNumBars = 1 + 2 * NKS + 2 * NVS + 2 + 2 + 3 + 3;
+  static constexpr int kNumBars = 1 + 2 * NKS + 2 * NVS + 2 + 2 + 3 + 2;
   static constexpr int kOffRed = (kOffBar + kNumBars * 8 + 16 + 15) / 16 * 16;
   // softmax exchange: row maxima [2 blocks][NG][128], row sums [2 tiles][NG][128]
   static constexpr int kSmemBytes = kOffRed + 4 * NG * 128 * 4 + 1024;
@@ -652,15 +652,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(NG), 1)
   // so no separate "O free" barrier is needed.
   const uint32_t bar_o_final = bar0 + 8u * (kB2 + 6);
   // Q staging buffer (this CTA's): q_smem_full completes when a tile's Q rows
-  // have landed (TMA, issued by the K producer); q_smem_free when they were
-  // copied into TMEM and the previous tile's O, written over them, has been
-  // stored out (warp 3), so the next tile's rows may be loaded.
+  // have landed (TMA, issued by warp 3 once the buffer is free).
   const uint32_t bar_q_smem_full = bar0 + 8u * (kB2 + 7);
-  const uint32_t bar_q_smem_free = bar0 + 8u * (kB2 + 8);
   // o_smem_full: the softmax warps are done with the buffer for one tile step
   // (this tile's Q copied into TMEM and the previous tile's O written over
-  // it); warp 3 then stores that O out and frees the buffer.
-  const uint32_t bar_o_smem_full = bar0 + 8u * (kB2 + 9);
+  // it); warp 3 then stores that O out and loads the next tile's Q into it.
+  const uint32_t bar_o_smem_full = bar0 + 8u * (kB2 + 8);
   const uint32_t sQ = sbase + C::kOffQ;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kOffBar + C::kNumBars * 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -727,8 +724,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(NG), 1)
     mbar_init(bar_o_done, 1);
     mbar_init(bar_drain, 1);
     mbar_init(bar_o_final, 1);
-    mbar_init(bar_q_smem_full, 1);
-    mbar_init(bar_q_smem_free, 1);  // warp 3
+    mbar_init(bar_q_smem_full, 1);  // warp 3
     mbar_init(bar_o_smem_full, 4 * NG);  // the softmax warps of this CTA
     *abort_flag = (*(volatile int*)p.err != 0) ? 1 : 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -755,24 +751,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(NG), 1)
     const int NS = is_k ? NKS : NVS;
     if (lane == 0 && !skip) {
       int G = 0;   // global key-block counter
-      int qit = 0;  // tiles whose Q rows were loaded (K producer)
       bool ok = true;
       for (int k = 0; k * n_clusters < n_work && ok; k++) {
         const int w = work_of(k);
         if (w >= n_work) continue;
         const Tile t = tile_of(w);
-        if (is_k) {
-          // This CTA's 128 rows of the tile's Q, as D/32 swizzled [128 x 32]
-          // chunks (rows past the slice read as zeros), once the previous
-          // tile's rows have been copied into TMEM.
-          if (qit > 0) ok = mbar_wait(bar_q_smem_free, (qit - 1) & 1, abort_flag, p.err);
-          if (!ok) break;
-          FA_EV(19, G);
-          mbar_expect_tx(bar_q_smem_full, C::kQBytes);
-          for (int c = 0; c < D / 32; c++)
-            tma_load_3d(sQ + c * (kBM * 128), &tmQ, bar_q_smem_full, 32 * c, t.q0, t.bh);
-          qit++;
-        }
         for (int j = 0; j < t.n_kv && ok; j++, G++) {
           const int s = G % NS;
           if (G >= NS)
@@ -802,7 +785,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(NG), 1)
         for (int g = max(0, G - NS); g < G; g++)
           mbar_wait(is_k ? bar_k_full(g % NS) : bar_v_full(g % NS), (g / NS) & 1, &no_abort,
                     p.err);
-      if (is_k && qit > 0) mbar_wait(bar_q_smem_full, (qit - 1) & 1, &no_abort, p.err);
     }
     __syncwarp();
   } else if (warp == 1) {
@@ -873,13 +855,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(NG), 1)
     }
     __syncwarp();
   } else if (warp == 3) {
-    // ------------------------------ O store (one lane): after the softmax warps
-    // are done with the buffer for a tile step, TMA-store the previous tile's O
-    // from it (rows past the slice are clipped by the tensor map), wait until
-    // the store has read it, and free it for the next tile's Q.
+    // ------------------------------ O store and Q load (one lane): after the
+    // softmax warps are done with the buffer for a tile step, TMA-store the
+    // previous tile's O from it (rows past the slice are clipped by the tensor
+    // map), wait until the store has read it, and load the next tile's Q into
+    // it at once, a whole tile ahead of its use.
     if (lane == 0 && !skip) {
       bool ok = true, have_prev = false;
-      int it = 0;
+      int it = 0, qit = 0;  // tile steps done, Q loads issued
       Tile pt{};
       auto store = [&](bool last) {
         if (pt.q_rows > 0)
@@ -891,20 +874,38 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(NG), 1)
         else
           bulk_wait_read_all();
       };
-      for (int k = 0; k * n_clusters < n_work && ok; k++) {
-        const int w = work_of(k);
-        if (w >= n_work) continue;
-        const Tile t = tile_of(w);
+      // This CTA's 128 rows of a tile's Q, as D/32 swizzled [128 x 32] chunks
+      // (rows past the slice read as zeros).
+      auto load_q = [&](const Tile& q) {
+        FA_EV(19, qit);
+        mbar_expect_tx(bar_q_smem_full, C::kQBytes);
+        for (int c = 0; c < D / 32; c++)
+          tma_load_3d(sQ + c * (kBM * 128), &tmQ, bar_q_smem_full, 32 * c, q.q0, q.bh);
+        qit++;
+      };
+      auto next_work = [&](int k) {  // the round after k that has a tile, or -1
+        for (int k2 = k + 1; k2 * n_clusters < n_work; k2++)
+          if (work_of(k2) < n_work) return k2;
+        return -1;
+      };
+      const int k0 = next_work(-1);
+      if (k0 >= 0) load_q(tile_of(work_of(k0)));
+      for (int k = k0; k >= 0 && ok; k = next_work(k)) {
+        const Tile t = tile_of(work_of(k));
         ok = mbar_wait(bar_o_smem_full, it & 1, abort_flag, p.err);
         if (!ok) break;
         if (have_prev) store(false);
         FA_EV(18, it);
-        mbar_arrive(bar_q_smem_free);
+        const int kn = next_work(k);
+        if (kn >= 0) load_q(tile_of(work_of(kn)));
         have_prev = true;
         pt = t;
         it++;
       }
       if (ok && have_prev && mbar_wait(bar_o_smem_full, it & 1, abort_flag, p.err)) store(true);
+      // no Q load may land after exit, even when a consumer role aborted
+      volatile int no_abort = 0;
+      if (qit > 0) mbar_wait(bar_q_smem_full, (qit - 1) & 1, &no_abort, p.err);
     }
     __syncwarp();
   } else if (warp >= kSoftmaxWarp0) {
