@@ -122,7 +122,12 @@ int dispatch(fa::FwdParams p, int dev, cudaStream_t s) {
   p.scale = 1.0f / sqrtf((float)p.d);
   p.scale_log2 = p.scale * 1.4426950408889634f;
   cudaError_t e = cudaSuccess;
-  if (p.sq <= 16 && fa::decode_supported(p.d)) {
+  // The tensor-core kernels address Q/K/V/O through TMA tensor maps and the
+  // decode kernel through 16-byte vector loads: both need 16-byte aligned
+  // bases.  A device call on other pointers (a view at an odd float offset)
+  // runs the CUDA-core f32 kernel, which reads floats one at a time.
+  const bool a16 = (((uintptr_t)p.q | (uintptr_t)p.k | (uintptr_t)p.v | (uintptr_t)p.o) & 15) == 0;
+  if (p.sq <= 16 && fa::decode_supported(p.d) && a16) {
     // Few query rows: split the key range so every SM streams K/V.
     t_path = "decode_splitkv";
     const int splits = fa::decode_pick_splits(p.bh, p.sq, p.sk, st.num_sms, p.d);
@@ -147,7 +152,7 @@ int dispatch(fa::FwdParams p, int dev, cudaStream_t s) {
     if (e != cudaSuccess) return cuda_err(e, "decode launch");
     return FA_OK;
   }
-  if (prec == FA_PREC_3XTF32 && (p.d == 64 || p.d == 128)) {
+  if (prec == FA_PREC_3XTF32 && (p.d == 64 || p.d == 128) && a16) {
     t_path = "tcgen05_3xtf32";
     float* ws = nullptr;
     e = cudaMallocAsync((void**)&ws, fa::tc3_workspace_floats(p, st.num_sms) * sizeof(float), s);
@@ -157,7 +162,7 @@ int dispatch(fa::FwdParams p, int dev, cudaStream_t s) {
     if (e != cudaSuccess) return cuda_err(e, "tcgen05 3xTF32 launch");
     return FA_OK;
   }
-  if (fa::tc_supported(p.d, prec)) {
+  if (fa::tc_supported(p.d, prec) && a16) {
     t_path = prec == FA_PREC_TF32 ? "tcgen05_tf32" : "tcgen05_3xtf32";
     // a launch with few 256-row tiles splits the key range (partials + LSE merge)
     const size_t nws = fa::tc_scratch_floats(p, st.num_sms);

@@ -7,9 +7,12 @@
 // f32 in TMEM; the dropped lo*lo term and the truncation of lo leave a relative
 // error near 2^-21, which keeps the output within 2e-5 of f32 attention.
 //
-//   K, V  split once per call by split_hi_lo into workspace planes (hi, lo),
-//         loaded by TMA like the TF32 kernel (K-major 128B swizzle for K,
-//         MN-major 128B/32B-atom swizzle for V).
+//   K, V  hi is read straight from K and V: the tensor core reads an f32
+//         operand of a kind::tf32 MMA by dropping its low 13 mantissa bits,
+//         which is exactly hi (the 2e-5 parity tests would show a rounding
+//         tensor core as a 2^-11 error).  lo is written once per call by
+//         split_lo into workspace planes.  All four load by TMA like the TF32
+//         kernel (K-major 128B swizzle for K, MN-major 128B/32B-atom for V).
 //   Q     split by the softmax warps and staged in TMEM: hi [0,D), lo [D,2D).
 //   P     written back to TMEM as hi (over S) and lo (next BK columns).
 //
@@ -23,22 +26,18 @@
 namespace fa {
 namespace {
 
-__global__ void __launch_bounds__(256) split_hi_lo(const float4* __restrict__ x,
-                                                   float4* __restrict__ hi,
-                                                   float4* __restrict__ lo, size_t n4) {
-  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4;
+// lo = x - hi for K and V ([0, n4) from k, [n4, 2 n4) from v), one pass.
+__global__ void __launch_bounds__(256) split_lo(const float4* __restrict__ k,
+                                                const float4* __restrict__ v,
+                                                float4* __restrict__ lo, size_t n4) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < 2 * n4;
        i += (size_t)gridDim.x * blockDim.x) {
-    const float4 v = x[i];
-    float4 h, l;
-    h.x = __uint_as_float(__float_as_uint(v.x) & 0xFFFFE000u);
-    h.y = __uint_as_float(__float_as_uint(v.y) & 0xFFFFE000u);
-    h.z = __uint_as_float(__float_as_uint(v.z) & 0xFFFFE000u);
-    h.w = __uint_as_float(__float_as_uint(v.w) & 0xFFFFE000u);
-    l.x = v.x - h.x;
-    l.y = v.y - h.y;
-    l.z = v.z - h.z;
-    l.w = v.w - h.w;
-    hi[i] = h;
+    const float4 x = i < n4 ? k[i] : v[i - n4];
+    float4 l;
+    l.x = x.x - __uint_as_float(__float_as_uint(x.x) & 0xFFFFE000u);
+    l.y = x.y - __uint_as_float(__float_as_uint(x.y) & 0xFFFFE000u);
+    l.z = x.z - __uint_as_float(__float_as_uint(x.z) & 0xFFFFE000u);
+    l.w = x.w - __uint_as_float(__float_as_uint(x.w) & 0xFFFFE000u);
     lo[i] = l;
   }
 }
@@ -389,22 +388,16 @@ template <int D, int BK, int NKS, int NVS, int NSB>
 cudaError_t launch_3x(const FwdParams& p, float* ws, int n_split, cudaStream_t s) {
   using C = Tc3Cfg<D, BK, NKS, NVS, NSB>;
   const size_t n = (size_t)p.bh * p.sk * D;  // floats per K (or V) plane
-  float* kh = ws;
-  float* kl = ws + n;
-  float* vh = ws + 2 * n;
-  float* vl = ws + 3 * n;
-  const int blocks = 148 * 8;
-  split_hi_lo<<<blocks, 256, 0, s>>>(reinterpret_cast<const float4*>(p.k),
-                                     reinterpret_cast<float4*>(kh), reinterpret_cast<float4*>(kl),
-                                     n / 4);
-  split_hi_lo<<<blocks, 256, 0, s>>>(reinterpret_cast<const float4*>(p.v),
-                                     reinterpret_cast<float4*>(vh), reinterpret_cast<float4*>(vl),
-                                     n / 4);
-  count_launch(2);
+  float* kl = ws;
+  float* vl = ws + n;
+  split_lo<<<148 * 8, 256, 0, s>>>(reinterpret_cast<const float4*>(p.k),
+                                   reinterpret_cast<const float4*>(p.v),
+                                   reinterpret_cast<float4*>(ws), n / 4);
+  count_launch(1);
   CUtensorMap mkh, mkl, mvh, mvl;
-  if (!make_map(&mkh, kh, D, p.sk, p.bh, BK, CU_TENSOR_MAP_SWIZZLE_128B) ||
+  if (!make_map(&mkh, p.k, D, p.sk, p.bh, BK, CU_TENSOR_MAP_SWIZZLE_128B) ||
       !make_map(&mkl, kl, D, p.sk, p.bh, BK, CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !make_map(&mvh, vh, D, p.sk, p.bh, BK, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B) ||
+      !make_map(&mvh, p.v, D, p.sk, p.bh, BK, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B) ||
       !make_map(&mvl, vl, D, p.sk, p.bh, BK, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B))
     return cudaErrorInvalidValue;
   static std::atomic<unsigned long long> attr_set{0};
@@ -419,7 +412,7 @@ cudaError_t launch_3x(const FwdParams& p, float* ws, int n_split, cudaStream_t s
     attr_set.fetch_or(bit);
   }
   const size_t rows = (size_t)p.bh * p.sq;
-  float* split_o = n_split > 1 ? ws + 4 * n : nullptr;
+  float* split_o = n_split > 1 ? ws + 2 * n : nullptr;
   float* split_lse = n_split > 1 ? split_o + (size_t)n_split * rows * D : nullptr;
   dim3 grid(p.bh, (p.sq + kBM - 1) / kBM, n_split);
   tc_fwd_3xtf32<D, BK, NKS, NVS, NSB><<<grid, kThreads, C::kSmemBytes, s>>>(mkh, mkl, mvh, mvl, p,
@@ -451,7 +444,7 @@ static int tc3_pick_splits(const FwdParams& p, int num_sms) {
 
 size_t tc3_workspace_floats(const FwdParams& p, int num_sms) {
   const int split = tc3_pick_splits(p, num_sms);
-  size_t f = 4 * (size_t)p.bh * p.sk * p.d;  // hi / lo planes of K and V
+  size_t f = 2 * (size_t)p.bh * p.sk * p.d;  // lo planes of K and V
   if (split > 1) f += (size_t)split * p.bh * p.sq * (p.d + 1);
   return f;
 }

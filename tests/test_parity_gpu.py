@@ -402,3 +402,32 @@ def test_key_range_split_of_small_launches(fa, prec, shape):
     want, wlse, _ = O.flash_v2_multihead(q, k, v, bh, sq, sk, d, causal)
     assert max_abs_diff(out, want) < TOL[prec]
     assert max_abs_diff(lse, wlse) < TOL[prec]
+
+
+@pytest.mark.parametrize("prec", [0, 1])
+@pytest.mark.parametrize("shape", [(2, 300, 300, 128, True), (3, 1, 2000, 64, False),
+                                   (2, 100, 700, 64, False)])
+def test_device_api_pointers_off_16_bytes(fa, prec, shape):
+    # Views one float into a buffer: the tensor-map and vector-load kernels need
+    # 16-byte aligned bases, so the call runs the CUDA-core f32 kernel.
+    import torch
+    bh, sq, sk, d, causal = shape
+    fa.set_precision(prec)
+    q, k, v = (random_vec(bh * sq * d, 71), random_vec(bh * sk * d, 72),
+               random_vec(bh * sk * d, 73))
+
+    def shifted(a, rows):
+        buf = torch.zeros(a.size + 1, device="cuda")
+        buf[1:].copy_(torch.from_numpy(a))
+        return buf[1:].view(bh, rows, d)
+
+    dq, dk, dv = shifted(q, sq), shifted(k, sk), shifted(v, sk)
+    dout = torch.full((bh * sq * d + 1,), float("nan"), device="cuda")[1:].view(bh, sq, d)
+    lse = torch.empty(bh, sq, device="cuda")
+    assert dq.data_ptr() % 16 != 0
+    fa.forward_device(dq, dk, dv, dout, lse, causal=causal)
+    torch.cuda.synchronize()
+    assert fa.last_path() == "simt_fp32"
+    want, wlse, _ = O.flash_v2_multihead(q, k, v, bh, sq, sk, d, causal)
+    assert max_abs_diff(dout.cpu().numpy().ravel(), want) < TOL[2]
+    assert max_abs_diff(lse.cpu().numpy().ravel(), wlse) < TOL[2]
