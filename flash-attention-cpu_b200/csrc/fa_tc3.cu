@@ -91,8 +91,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int bh = blockIdx.x;
-  const int qt = (int)gridDim.y - 1 - (int)blockIdx.y;
+  // blockIdx.x runs over (slice, tile).  Causal: heaviest tiles of all
+  // slices first, for the balance of the last wave.  Non-causal tiles cost the
+  // same, so the tiles of a slice are adjacent and the CTAs resident at one
+  // time share few slices' K/V planes through L2 (measured on one B200:
+  // 256 x 1024 x 64 142 -> 165 TFLOP/s; the slice-adjacent order on the causal
+  // 32 x 4096 x 128 ran 186 -> 165, its heavy tiles landing in the last wave).
+  const int n_qt = (p.sq + kBM - 1) / kBM;
+  const unsigned lin = blockIdx.x;
+  const int bh = p.causal ? (int)(lin % (unsigned)p.bh) : (int)(lin / (unsigned)n_qt);
+  const int qt = p.causal ? n_qt - 1 - (int)(lin / (unsigned)p.bh) : (int)(lin % (unsigned)n_qt);
   const int q0 = qt * kBM;
   const int q_rows = min(kBM, p.sq - q0);
   int kend = p.sk;
@@ -104,7 +112,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int j0 = (int)((long long)blockIdx.z * nb / gridDim.z);
   const int n_kv = (int)((long long)(blockIdx.z + 1) * nb / gridDim.z) - j0;
   const bool to_split = gridDim.z > 1;
-  const size_t zrow = (size_t)(blockIdx.z * gridDim.x + bh) * p.sq;  // row base in split space
+  const size_t zrow = ((size_t)blockIdx.z * p.bh + bh) * p.sq;  // row base in split space
 
   if (threadIdx.x == 0) {
     mbar_init(bar_q_full, 128);
@@ -414,7 +422,9 @@ cudaError_t launch_3x(const FwdParams& p, float* ws, int n_split, cudaStream_t s
   const size_t rows = (size_t)p.bh * p.sq;
   float* split_o = n_split > 1 ? ws + 2 * n : nullptr;
   float* split_lse = n_split > 1 ? split_o + (size_t)n_split * rows * D : nullptr;
-  dim3 grid(p.bh, (p.sq + kBM - 1) / kBM, n_split);
+  const long long n_ctas = (long long)p.bh * ((p.sq + kBM - 1) / kBM);
+  if (n_ctas > INT32_MAX) return cudaErrorInvalidValue;
+  dim3 grid((unsigned)n_ctas, 1, n_split);
   tc_fwd_3xtf32<D, BK, NKS, NVS, NSB><<<grid, kThreads, C::kSmemBytes, s>>>(mkh, mkl, mvh, mvl, p,
                                                                             split_o, split_lse);
   count_launch();
@@ -450,7 +460,6 @@ size_t tc3_workspace_floats(const FwdParams& p, int num_sms) {
 }
 
 cudaError_t launch_tc3(const FwdParams& p, float* ws, int num_sms, cudaStream_t s) {
-  if (p.sq > 65535 * kBM) return cudaErrorInvalidValue;
   const int split = tc3_pick_splits(p, num_sms);
   if (p.d == 128) return launch_3x<128, 64, 2, 1, 1>(p, ws, split, s);
   if (p.d == 64) return launch_3x<64, 64, 3, 3, 2>(p, ws, split, s);
