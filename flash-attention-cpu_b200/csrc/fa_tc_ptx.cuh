@@ -226,6 +226,23 @@ __device__ __forceinline__ uint32_t to_tf32_rna(float x) {
   asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
   return r;
 }
+// Named barrier over `n` threads that also ORs a per-thread flag: every
+// participant gets the same result, so a failure seen by any of them makes all
+// of them leave a loop together (a plain bar.sync would leave the others
+// waiting forever).
+__device__ __forceinline__ bool bar_any(uint32_t id, uint32_t n, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred pi, po;\n\t"
+      "setp.ne.u32 pi, %1, 0;\n\t"
+      "bar.red.or.pred po, %2, %3, pi;\n\t"
+      "selp.u32 %0, 1, 0, po;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)v), "r"(id), "r"(n)
+      : "memory");
+  return r != 0;
+}
+
 __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
