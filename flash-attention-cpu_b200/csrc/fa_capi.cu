@@ -214,6 +214,10 @@ int check_err_flag(int dev, cudaStream_t s) {
 // the copies of the others (the two copy directions use separate engines).
 struct HostCallStreams {
   cudaStream_t s[kMaxDevices][3] = {};
+  // events of the chunked pipeline and a pinned word for the device error
+  // flag, kept for the thread's next call
+  cudaEvent_t ev[kMaxDevices][2 * 8 + 2] = {};
+  int* err_host[kMaxDevices] = {};
 };
 thread_local HostCallStreams t_streams;
 
@@ -371,18 +375,23 @@ int host_forward(const float* q, const float* k, const float* v, size_t bh, size
                                s_out);
   const size_t n_chunks = (bh >= 2 && bytes >= (size_t(32) << 20)) ? (bh < 8 ? bh : 8) : 1;
   const size_t per = (bh + n_chunks - 1) / n_chunks;
+  cudaEvent_t* ev = t_streams.ev[dev];
+  const int n_ev = (int)(2 * n_chunks + 2);
+  cudaError_t e = cudaSuccess;
+  for (int i = 0; i < n_ev && e == cudaSuccess; i++)
+    if (!ev[i]) e = cudaEventCreateWithFlags(&ev[i], cudaEventDisableTiming);
+  if (e == cudaSuccess && !t_streams.err_host[dev])
+    e = cudaMallocHost((void**)&t_streams.err_host[dev], sizeof(int));
+  if (e != cudaSuccess) return cuda_err(e, "host call events");
+  int* err_h = t_streams.err_host[dev];
   char* buf = nullptr;
-  cudaError_t e = cudaMallocAsync((void**)&buf, bytes, s_in);
+  e = cudaMallocAsync((void**)&buf, bytes, s_in);
   if (e != cudaSuccess) return cuda_err(e, "cudaMallocAsync(staging)");
   float* dq = (float*)buf;
   float* dk = dq + nq;
   float* dv = dk + nk;
   float* dout = dv + nk;
   float* dlse = dout + nq;
-  cudaEvent_t ev[2 * 8 + 1];
-  int n_ev = 0;
-  for (size_t i = 0; i < 2 * n_chunks + 1 && e == cudaSuccess; i++, n_ev++)
-    e = cudaEventCreateWithFlags(&ev[i], cudaEventDisableTiming);
   for (size_t c = 0; c < n_chunks && e == cudaSuccess && rc == FA_OK; c++) {
     const size_t h0 = c * per, h1 = (h0 + per < bh) ? h0 + per : bh;
     if (h0 >= h1) break;
@@ -411,17 +420,29 @@ int host_forward(const float* q, const float* k, const float* v, size_t bh, size
       e = cudaMemcpyAsync(lse + h0 * sq, dlse + h0 * sq, (h1 - h0) * sq * sizeof(float),
                           cudaMemcpyDeviceToHost, s_out);
   }
-  // everything done before the staging buffer is freed on s_in
-  cudaError_t e2 = cudaEventRecord(ev[n_ev - 1], s_out);
+  // The device error word comes back behind the outputs (s_out waited for the
+  // last kernel), and one synchronisation covers both.  The staging buffer is
+  // freed in stream order once s_out and s_comp are done with it.
+  *err_h = 0;
+  cudaError_t e2 = cudaMemcpyAsync(err_h, g_dev[dev].err_flag, sizeof(int),
+                                   cudaMemcpyDeviceToHost, s_out);
+  if (e2 == cudaSuccess) e2 = cudaEventRecord(ev[n_ev - 2], s_out);
+  if (e2 == cudaSuccess) e2 = cudaEventRecord(ev[n_ev - 1], s_comp);
+  if (e2 == cudaSuccess) e2 = cudaStreamWaitEvent(s_in, ev[n_ev - 2], 0);
   if (e2 == cudaSuccess) e2 = cudaStreamWaitEvent(s_in, ev[n_ev - 1], 0);
+  cudaFreeAsync(buf, s_in);
   cudaError_t e3 = cudaStreamSynchronize(s_out);
-  cudaStreamSynchronize(s_comp);
+  if (e2 != cudaSuccess) {  // (the ordering above failed: drain everything)
+    cudaStreamSynchronize(s_comp);
+    cudaStreamSynchronize(s_in);
+  }
   if (e == cudaSuccess) e = e2 != cudaSuccess ? e2 : e3;
   if (rc == FA_OK && e != cudaSuccess) rc = cuda_err(e, "host staging");
-  if (rc == FA_OK) rc = check_err_flag(dev, s_in);
-  cudaFreeAsync(buf, s_in);
-  cudaStreamSynchronize(s_in);
-  for (int i = 0; i < n_ev; i++) cudaEventDestroy(ev[i]);
+  if (rc == FA_OK && *err_h != 0) {
+    cudaMemsetAsync(g_dev[dev].err_flag, 0, sizeof(int), s_out);
+    cudaStreamSynchronize(s_out);
+    rc = set_err(FA_ERR_TIMEOUT, "a bounded in-kernel wait expired (kernel aborted)");
+  }
   return rc;
 }
 
