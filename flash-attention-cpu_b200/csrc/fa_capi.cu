@@ -772,14 +772,29 @@ int fa_unpin_host(void* ptr) {
 
 void fa_shutdown(void) {
   fa::staging_release_all();
-  for (int d = 0; d < kMaxDevices; d++)
+  // the calling thread's streams, pipeline events and pinned error word
+  for (int d = 0; d < kMaxDevices; d++) {
+    bool set = false;
     for (int i = 0; i < 3; i++)
       if (t_streams.s[d][i]) {
-        cudaSetDevice(d);
+        if (!set) cudaSetDevice(d);
+        set = true;
         cudaStreamSynchronize(t_streams.s[d][i]);
         cudaStreamDestroy(t_streams.s[d][i]);
         t_streams.s[d][i] = nullptr;
       }
+    for (cudaEvent_t& e : t_streams.ev[d])
+      if (e) {
+        if (!set) cudaSetDevice(d);
+        set = true;
+        cudaEventDestroy(e);
+        e = nullptr;
+      }
+    if (t_streams.err_host[d]) {
+      cudaFreeHost(t_streams.err_host[d]);
+      t_streams.err_host[d] = nullptr;
+    }
+  }
 }
 
 }  // extern "C"

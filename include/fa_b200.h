@@ -222,7 +222,8 @@ FA_API const char* fa_last_path(void);
 FA_API int fa_pin_host(void* ptr, size_t bytes);
 /* Undoes fa_pin_host (`ptr` as given to it). */
 FA_API int fa_unpin_host(void* ptr);
-/* Frees cached device workspaces and staging buffers. */
+/* Frees cached staging buffers, and the calling thread's streams, events and
+ * pinned status word (created again on the next call). */
 FA_API void fa_shutdown(void);
 
 #ifdef __cplusplus

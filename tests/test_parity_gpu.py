@@ -431,3 +431,22 @@ def test_device_api_pointers_off_16_bytes(fa, prec, shape):
     want, wlse, _ = O.flash_v2_multihead(q, k, v, bh, sq, sk, d, causal)
     assert max_abs_diff(dout.cpu().numpy().ravel(), want) < TOL[2]
     assert max_abs_diff(lse.cpu().numpy().ravel(), wlse) < TOL[2]
+
+
+def test_calls_after_fa_shutdown(fa):
+    # fa_shutdown frees the staging rings and the calling thread's streams,
+    # events and status word; the next calls create them again.
+    import ctypes
+    L = fa._load()
+    L.fa_shutdown.restype = None
+    fa.set_precision(0)
+    for bh, s, d in ((2, 300, 64), (8, 1024, 128)):  # the small path, then the staged one
+        q, k, v = (random_vec(bh * s * d, 81 + i) for i in range(3))
+        cfg = fa.FlashAttentionConfig(64, 128, True)
+        a = np.zeros(bh * s * d, np.float32)
+        fa.flash_attention_multihead_v2(q, k, v, 1, bh, s, s, d, cfg, a)
+        L.fa_shutdown()
+        b = np.full(bh * s * d, np.nan, np.float32)
+        fa.flash_attention_multihead_v2(q, k, v, 1, bh, s, s, d, cfg, b)
+        assert np.array_equal(a, b)
+        L.fa_shutdown()
