@@ -450,3 +450,26 @@ def test_calls_after_fa_shutdown(fa):
         fa.flash_attention_multihead_v2(q, k, v, 1, bh, s, s, d, cfg, b)
         assert np.array_equal(a, b)
         L.fa_shutdown()
+
+
+@pytest.mark.parametrize("prec", [0, 1])
+@pytest.mark.parametrize("causal", [False, True])
+def test_rising_scores_rescale_every_block(fa, prec, causal):
+    # Q all ones and K rows j/64 (exact in TF32): the score of key j is j / 8
+    # before scaling, so every 128-key block raises the row maximum by ~23
+    # log2 units and takes the rescale path of O and l (P recomputed against
+    # the new maximum).  The output is a weighted mean of the last few V rows.
+    bh, sq, sk, d = 2, 300, 1024, 64
+    fa.set_precision(prec)
+    q = np.ones(bh * sq * d, np.float32)
+    kr = (np.arange(sk, dtype=np.float32) / 64.0)[:, None] * np.ones((1, d), np.float32)
+    k = np.tile(kr.ravel(), bh).astype(np.float32)
+    v = random_vec(bh * sk * d, 97)
+    out, lse = fa.multihead_lse(q, k, v, bh, sq, sk, d, causal)
+    want, wlse, _ = O.flash_v2_multihead(q, k, v, bh, sq, sk, d, causal)
+    assert np.all(np.isfinite(out))
+    assert max_abs_diff(out, want) < TOL[prec]
+    # the LSE carries the rounding of the prescaled Q (TF32: 2^-12 relative)
+    # times scores near 40 log2 units; 3xTF32 is compensated
+    rel = 2.0 ** -10 if prec == 0 else 1e-4
+    assert max_abs_diff(lse, wlse) < rel * (1 + np.max(np.abs(wlse)))
