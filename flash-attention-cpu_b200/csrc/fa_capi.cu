@@ -771,6 +771,8 @@ int fa_unpin_host(void* ptr) {
 }
 
 void fa_shutdown(void) {
+  int cur = 0;
+  const bool have_cur = cudaGetDevice(&cur) == cudaSuccess;
   fa::staging_release_all();
   // the calling thread's streams, pipeline events and pinned error word
   for (int d = 0; d < kMaxDevices; d++) {
@@ -795,6 +797,7 @@ void fa_shutdown(void) {
       t_streams.err_host[d] = nullptr;
     }
   }
+  if (have_cur) cudaSetDevice(cur);  // the caller's device, as it was
 }
 
 }  // extern "C"
