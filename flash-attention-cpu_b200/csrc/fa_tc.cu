@@ -565,7 +565,6 @@ __device__ __forceinline__ void cluster_sync_all() {
                    : "memory");
 }
 
-
 template <int D, int BK, int NKS, int NVS, int NG>
 struct PairCfg {
   static constexpr int kKHalf = BK / 2;                 // keys of a K tile held per CTA
