@@ -1,39 +1,53 @@
 // Tensor-core attention forward for sm_100a (B200): tcgen05 TF32 MMAs with
 // the accumulators in tensor memory (TMEM), TMA tile loads into 128-byte
 // swizzled shared memory, and warp-specialised roles on an mbarrier pipeline.
+// Two kernels share the design:
 //
-// One CTA computes one 128-row query tile of one (batch, head) slice:
-//   warp 0 (one lane)  TMA producer: Q tile once, then K and V tiles of BK keys
-//                      through an NS-deep ring (separate K and V slots so a K
-//                      slot frees as soon as its QK^T MMA has read it).
-//   warp 1 (one lane)  MMA issuer: S_b = Q K_j^T into TMEM buffer b = j%2, then
+// tc_fwd_tf32 (up to 128 query rows): one CTA per 128-row tile of a slice,
+// with blockIdx.z parts of the key range for launches that leave SMs idle.
+//   warp 0 (one lane)  K producer: K tiles of BK keys through an NKS-deep ring.
+//   warp 2 (one lane)  V producer: V sub-tiles of VK keys through an NVS-deep
+//                      ring (separate rings, so a K slot frees as soon as its
+//                      QK^T MMA has read it, before PV).
+//   warp 1             MMA issuer (warp-uniform, one elected lane issues):
+//                      S_b = Q K_j^T into TMEM buffer b = j % 2, then
 //                      O += P_{j-1} V_{j-1} with P read straight from TMEM
 //                      (the .kind::tf32 "A from TMEM" form).  Issuing S_j
 //                      before PV_{j-1} lets QK^T of the next tile run while the
 //                      softmax warps work on the current one (the mechanism
 //                      behind the crate's v3 software pipelining,
 //                      src/v3.rs:445-483).
-//   warps 4-7          softmax, one query row per thread: tcgen05.ld the score
-//                      row, mask (causal diagonal tiles and keys past seq_len_k,
-//                      src/v2.rs:268-287), running max, exp2, row sum, P written
-//                      back over S in TMEM (src/v2.rs:289-339).  O is rescaled
-//                      in TMEM only when the running max grows by more than
-//                      2^8 (lazy rescaling); O and l share the same stale max,
-//                      so the final out = O / l (src/v2.rs:375-382) is exact.
-// Causal runs never load or multiply key tiles wholly past the tile's last
-// row (src/v2.rs:210-212), and CTAs are dispatched heaviest-tile first.
+//   warps 4-7          softmax, one query row per thread: Q staged into TMEM
+//                      (scaled by scale*log2 e, rounded to TF32), then per
+//                      tile tcgen05.ld the score row, mask (causal diagonal
+//                      tiles and keys past seq_len_k, src/v2.rs:268-287),
+//                      running max, exp2, row sum, P written back over S in
+//                      TMEM (src/v2.rs:289-339).  O is rescaled in TMEM only
+//                      when the running max grows by more than 2^8 (lazy
+//                      rescaling); O and l share the same stale max, so the
+//                      final out = O / l (src/v2.rs:375-382) is exact.
+//   TMEM columns: Q [0, D), O [D, 2D), S/P buffers [2D + b*BK, 2D + (b+1)*BK).
+//
+// tc_fwd_tf32_pair (more than 128 query rows): a persistent CTA pair
+// (cta_group::2, M = 256) per SM pair looping over 256-row work tiles; each SM
+// holds half of every K tile and half of every V tile's columns.  Warp 3 moves
+// O out and the next tile's Q in through one shared-memory buffer, and two
+// softmax warpgroups split each row's columns.  The kernel's own comment has
+// the details.
+//
+// Causal runs never load or multiply key tiles wholly past a tile's last row
+// (src/v2.rs:210-212), and the heaviest tiles are dispatched first.
 //
 // Shared-memory layouts (all 1024-byte aligned, 32 f32 = 128 B per swizzle row):
-//   Q  [D/32 chunks][128 rows][32]   K-major A operand of QK^T, 128B swizzle
+//   K  [D/32 chunks][BK keys][32]    K-major B operand of QK^T, 128B swizzle
 //                                    (16-byte granules XOR row%8)
-//   K  [D/32 chunks][BK keys][32]    K-major B operand of QK^T, same swizzle
-//   V  [D/32 chunks][BK keys][32]    MN-major B operand of PV (d contiguous).
+//   V  [D/32 chunks][VK keys][32]    MN-major B operand of PV (d contiguous).
 //                                    An MN-major TF32 operand must use the
 //                                    "128B swizzle, 32B atom" layout (32-byte
 //                                    granules XOR row%4; K grouped by 4 rows,
 //                                    512 B apart), which TMA writes with
 //                                    CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B.
-// TMEM columns: O at [0, D), S/P buffer b at [D + b*BK, D + (b+1)*BK).
+//   Q / O (pair kernel) [D/32 chunks][128 rows][32], 128B swizzle.
 #include "fa_tc_ptx.cuh"
 
 namespace fa {
@@ -605,7 +619,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(NG), 1)
   // while the current one finishes.  Each CTA's Q rows arrive by TMA in a
   // shared-memory buffer a tile ahead; at a tile change the softmax warps copy
   // them into TMEM (scaled, TF32-rounded), then write the finished tile's O
-  // over them, and warp 3 stores that O by TMA and frees the buffer.
+  // over them, and warp 3 stores that O by TMA and loads the next tile's Q
+  // into the buffer.
   using C = PairCfg<D, BK, NKS, NVS, NG>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
