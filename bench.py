@@ -236,11 +236,14 @@ def run_reference(args):
     vals = []
     base = None
     # Each step is a bounded sample and the whole run stays within ~2 minutes:
-    # the per-step budget shrinks with the step count down to one slice (or
-    # one block of query rows), and once REF_WALL_S have passed the remaining
-    # steps are not run (every step samples the same workload and the line
-    # reports a rate; the steps actually timed are in cpu_baseline).
-    per_step = min(args.ref_budget, 120.0 / (args.warmup + args.steps))
+    # the per-step budget shrinks with the step count, and once REF_WALL_S
+    # have passed the remaining steps are not run (every step samples the same
+    # workload and the line reports a rate; the steps actually timed are in
+    # cpu_baseline).
+    # (at least ~1 s per step, so that a step times whole batches of slices at
+    # the rate a long run sees: one-slice samples of ~20 ms measured ~20 %
+    # slower per FLOP)
+    per_step = min(args.ref_budget, max(1.0, 120.0 / (args.warmup + args.steps)))
     t_start = time.perf_counter()
     for i in range(args.warmup + args.steps):
         b = cpu_baseline(cfg, budget_s=per_step)
