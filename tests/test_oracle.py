@@ -104,3 +104,31 @@ def test_multithreaded_driver_matches_single_thread():
                           v[h * sk * d:(h + 1) * sk * d], sq, sk, d, True)
         assert np.array_equal(a[h * sq * d:(h + 1) * sq * d], o)
         assert np.array_equal(la[h * sq:(h + 1) * sq], l)
+
+
+@pytest.mark.parametrize("sq,sk,d,causal", [(70, 90, 32, True), (90, 70, 64, False),
+                                            (128, 300, 16, True), (1, 257, 8, False)])
+def test_lse_matches_f64_logsumexp(sq, sk, d, causal):
+    # the row log-sum-exp the restatement adds (m_i + ln l_i of the scaled
+    # scores, the value the GPU kernels return beside O) against float64
+    q, k, v = random_vec(sq * d, 11), random_vec(sk * d, 12), random_vec(sk * d, 13)
+    _, lse = O.flash_v2(q, k, v, sq, sk, d, causal)
+    s = (q.reshape(sq, d).astype(np.float64) @ k.reshape(sk, d).astype(np.float64).T) / np.sqrt(d)
+    if causal:
+        s = np.where(np.arange(sk)[None, :] <= np.arange(sq)[:, None], s, -np.inf)
+    mx = s.max(axis=1, keepdims=True)
+    want = (mx + np.log(np.exp(s - mx).sum(axis=1, keepdims=True))).ravel()
+    assert np.max(np.abs(lse - want)) < 1e-5 * (1 + np.max(np.abs(want)))
+
+
+def test_partial_run_matches_full_run_on_its_rows():
+    # max_items limits the driver to the first 64-row query blocks (bench.py
+    # samples the config-5 head this way); those rows equal a full run's
+    bh, sq, sk, d = 1, 300, 300, 32
+    q, k, v = random_vec(sq * d, 21), random_vec(sk * d, 22), random_vec(sk * d, 23)
+    full, lf, n_full = O.flash_v2_multihead(q, k, v, bh, sq, sk, d, True, nthreads=2)
+    part, lp, n_part = O.flash_v2_multihead(q, k, v, bh, sq, sk, d, True, nthreads=2,
+                                            max_items=2)
+    assert n_full == (sq + 63) // 64 and n_part == 2
+    assert np.array_equal(part[:128 * d], full[:128 * d])
+    assert np.array_equal(lp[:128], lf[:128])
