@@ -104,3 +104,33 @@ def test_precision_control():
             fa_b200.set_precision(7)
     finally:
         fa_b200.set_precision(old)
+
+
+def test_device_entry_points_validate_before_any_device_call():
+    # fa_forward_device / fa_backward_device check their arguments first, the
+    # same on a host without a GPU: zero sizes return at once, null buffers
+    # and d_head > 256 are argument errors.
+    L = fa_b200._load()
+    buf = (ctypes.c_float * 64)()
+    p = ctypes.cast(buf, ctypes.c_void_p)
+    FA_OK, FA_ERR_ARG, FA_ERR_UNSUPPORTED = 0, 2, 6
+    assert L.fa_forward_device(p, p, p, p, None, 0, 4, 4, 8, 0, None) == FA_OK
+    assert L.fa_forward_device(p, p, p, p, None, 1, 0, 4, 8, 0, None) == FA_OK
+    assert L.fa_forward_device(None, p, p, p, None, 1, 4, 4, 8, 0, None) == FA_ERR_ARG
+    assert L.fa_forward_device(p, p, p, None, None, 1, 4, 4, 8, 0, None) == FA_ERR_ARG
+    assert L.fa_forward_device(p, p, p, p, None, 1, 4, 4, 257, 0, None) == FA_ERR_UNSUPPORTED
+    L.fa_backward_device.restype = ctypes.c_int
+    assert L.fa_backward_device(p, p, p, p, p, p, p, p, p, 0, 4, 4, 8, 0, None) == FA_OK
+    assert L.fa_backward_device(p, p, p, p, None, p, p, p, p, 1, 4, 4, 8, 0, None) == FA_ERR_ARG
+    assert L.fa_backward_device(p, p, p, p, p, p, p, p, p, 1, 4, 4, 129, 0,
+                                None) == FA_ERR_UNSUPPORTED
+
+
+def test_python_device_api_checks_tensors():
+    torch = pytest.importorskip("torch")
+    q = torch.zeros(2, 4, 8)
+    k = torch.zeros(2, 6, 8)
+    with pytest.raises(fa_b200.Panic):  # out shaped like k, not like q
+        fa_b200.forward_device(q, k, k, torch.zeros(2, 6, 8))
+    with pytest.raises(TypeError, match="CUDA tensor"):  # host tensors
+        fa_b200.forward_device(q, k, k, torch.zeros(2, 4, 8))
