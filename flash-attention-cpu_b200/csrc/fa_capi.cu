@@ -666,15 +666,25 @@ int fa_forward_decode_noalloc(const float* q, const float* k, const float* v, fl
   t_err.clear();
   if (bh == 0 || sq == 0 || sk == 0 || d == 0) return FA_OK;
   if (!q || !k || !v || !out) return set_err(FA_ERR_ARG, "null buffer pointer");
-  if (sq > 16 || !fa::decode_supported((int)d))
+  // Sizes are checked on their size_t values, before any narrowing cast.
+  if (sq > 16 || d > 256 || !fa::decode_supported((int)d))
     return set_err(FA_ERR_UNSUPPORTED,
                    "fa_forward_decode_noalloc handles seq_len_q <= 16 and d_head % 4 == 0, "
                    "d_head <= 256");
-  if (bh > 65535 || sk > (size_t)INT32_MAX)
-    return set_err(FA_ERR_UNSUPPORTED, "fa_forward_decode_noalloc: batch_heads > 65535");
-  // Device checks without the library's lazy set-up (which allocates).
-  int dev = 0, major = 0, sms = 0;
-  cudaError_t e = cudaGetDevice(&dev);
+  if (bh > 65535) return set_err(FA_ERR_UNSUPPORTED, "fa_forward_decode_noalloc: batch_heads > 65535");
+  if (sk > (size_t)INT32_MAX)
+    return set_err(FA_ERR_UNSUPPORTED, "fa_forward_decode_noalloc: seq_len_k > 2147483647");
+  // The decode kernel reads Q, K and V with 16-byte vector loads; the regular
+  // entry point sends other pointers to the scalar kernel, this one refuses
+  // them before any device call.
+  if ((((uintptr_t)q | (uintptr_t)k | (uintptr_t)v | (uintptr_t)out) & 15) != 0 ||
+      ((uintptr_t)lse & 3) != 0)
+    return set_err(FA_ERR_UNSUPPORTED,
+                   "fa_forward_decode_noalloc: q, k, v and out must be 16-byte aligned");
+  // Device checks without the library's lazy set-up (which allocates).  The
+  // device chosen by fa_set_device applies here as in every other call.
+  int dev = g_device.load(), major = 0, sms = 0;
+  cudaError_t e = dev >= 0 ? cudaSetDevice(dev) : cudaGetDevice(&dev);
   if (e == cudaSuccess) e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
   if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   if (e != cudaSuccess) {

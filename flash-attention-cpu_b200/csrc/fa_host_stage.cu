@@ -116,12 +116,34 @@ bool is_pageable(const void* p) {
   return a.type == cudaMemoryTypeUnregistered;
 }
 
+// Frees whatever a ring holds (slots and events created so far).
+static void ring_free(PinnedRing& r) {
+  for (int i = 0; i < PinnedRing::kSlots; i++) {
+    if (r.ev[i]) {
+      cudaEventSynchronize(r.ev[i]);
+      cudaEventDestroy(r.ev[i]);
+      r.ev[i] = nullptr;
+    }
+    if (r.buf[i]) {
+      cudaFreeHost(r.buf[i]);
+      r.buf[i] = nullptr;
+    }
+    r.busy[i] = false;
+  }
+  r.next = 0;
+}
+
+// All slots of a ring, or none: on a failure the slots and events already
+// created are freed again, so a later call starts from an empty ring.
 static cudaError_t ring_init(PinnedRing& r) {
   for (int i = 0; i < PinnedRing::kSlots; i++) {
     cudaError_t e = cudaMallocHost((void**)&r.buf[i], PinnedRing::kSlotBytes);
-    if (e != cudaSuccess) return e;
-    e = cudaEventCreateWithFlags(&r.ev[i], cudaEventDisableTiming);
-    if (e != cudaSuccess) return e;
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&r.ev[i], cudaEventDisableTiming);
+    if (e != cudaSuccess) {
+      cudaGetLastError();  // clear the (non-sticky) error of the failed call
+      ring_free(r);
+      return e;
+    }
     r.busy[i] = false;
   }
   r.next = 0;
@@ -134,7 +156,10 @@ cudaError_t staging_acquire(int dev, PinnedRing** in, PinnedRing** out, std::mut
   g.call.lock();
   if (!g.ready) {
     cudaError_t e = ring_init(g.in);
-    if (e == cudaSuccess) e = ring_init(g.out);
+    if (e == cudaSuccess) {
+      e = ring_init(g.out);
+      if (e != cudaSuccess) ring_free(g.in);
+    }
     if (e != cudaSuccess) {
       g.call.unlock();
       return e;
@@ -152,13 +177,8 @@ void staging_release_all() {
     std::lock_guard<std::mutex> lk(g.call);
     if (!g.ready) continue;
     cudaSetDevice(d);
-    for (PinnedRing* r : {&g.in, &g.out})
-      for (int i = 0; i < PinnedRing::kSlots; i++) {
-        cudaEventSynchronize(r->ev[i]);
-        cudaEventDestroy(r->ev[i]);
-        cudaFreeHost(r->buf[i]);
-        r->buf[i] = nullptr;
-      }
+    ring_free(g.in);
+    ring_free(g.out);
     g.ready = false;
   }
 }

@@ -171,8 +171,11 @@ FA_API int fa_lse_combine_device(const float* o_parts, const float* lse_parts, s
  * FA_ERR_UNSUPPORTED.  The first call on a device looks the array's address
  * up (a CUDA runtime query, no allocation); make that first call before any
  * stream capture.  All calls on a device share the array: calls whose kernels
- * overlap on the GPU race (serialise them on one stream).  Device buffers,
- * asynchronous on `stream`. */
+ * overlap on the GPU race (serialise them on one stream).  q, k, v and out
+ * must be 16-byte aligned (the kernel reads them with 16-byte vector loads);
+ * other pointers are refused with FA_ERR_UNSUPPORTED before any device call.
+ * The device set by fa_set_device applies, as for every other call.  Device
+ * buffers, asynchronous on `stream`. */
 FA_API int fa_forward_decode_noalloc(const float* q, const float* k, const float* v, float* out,
                                      float* lse, size_t batch_heads, size_t seq_len_q,
                                      size_t seq_len_k, size_t d_head, int causal, void* stream);

@@ -134,3 +134,33 @@ def test_python_device_api_checks_tensors():
         fa_b200.forward_device(q, k, k, torch.zeros(2, 6, 8))
     with pytest.raises(TypeError, match="CUDA tensor"):  # host tensors
         fa_b200.forward_device(q, k, k, torch.zeros(2, 4, 8))
+
+
+def test_noalloc_refuses_before_any_device_call():
+    # fa_forward_decode_noalloc checks sizes on their size_t values and the
+    # 16-byte alignment its vector loads need before it touches a device, so
+    # these refusals are the same on a host without a GPU, and launch nothing.
+    L = fa_b200._load()
+    buf = (ctypes.c_float * 1024)()
+    base = ctypes.addressof(buf)
+    a16 = (base + 15) & ~15
+    p = ctypes.c_void_p(a16)
+    odd = ctypes.c_void_p(a16 + 4)  # one float into the buffer
+    FA_OK, FA_ERR_UNSUPPORTED = 0, 6
+    n0 = fa_b200.launch_count()
+    assert L.fa_forward_decode_noalloc(p, p, p, p, None, 0, 1, 4, 8, 0, None) == FA_OK
+    for args in ((odd, p, p, p), (p, odd, p, p), (p, p, odd, p), (p, p, p, odd)):
+        assert L.fa_forward_decode_noalloc(*args, None, 1, 1, 4, 8, 0, None) == FA_ERR_UNSUPPORTED
+        assert b"16-byte aligned" in L.fa_last_error()
+    # d_head beyond 32 bits must not wrap to an accepted value
+    assert L.fa_forward_decode_noalloc(p, p, p, p, None, 1, 1, 4, (1 << 32) + 8, 0,
+                                       None) == FA_ERR_UNSUPPORTED
+    assert L.fa_forward_decode_noalloc(p, p, p, p, None, 1, 17, 4, 8, 0,
+                                       None) == FA_ERR_UNSUPPORTED
+    assert L.fa_forward_decode_noalloc(p, p, p, p, None, 65536, 1, 4, 8, 0,
+                                       None) == FA_ERR_UNSUPPORTED
+    assert b"batch_heads" in L.fa_last_error()
+    assert L.fa_forward_decode_noalloc(p, p, p, p, None, 1, 1, 1 << 31, 8, 0,
+                                       None) == FA_ERR_UNSUPPORTED
+    assert b"seq_len_k" in L.fa_last_error()
+    assert fa_b200.launch_count() == n0
