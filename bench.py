@@ -4,14 +4,23 @@ Metric: attention TFLOP/s, algorithmic FLOPs = 4*Sq*Sk*d per
 (batch, head) slice, halved when causal, as a fraction of the dense TF32
 roofline.  A step is one forward over one batch of the workload with its
 inputs resident in HBM.  Default workload
-(32 heads x 4096 x 128, causal, N(0,1)*0.5 from seed 1), f32 inputs,
-TF32 tensor-core arithmetic.  Inputs (268 MB) are larger than the 126 MB L2, so
-no flush is needed between steps.
+(32 heads x 4096 x 128, causal), TF32 tensor-core arithmetic, inputs from
+BASELINE's generator: numpy default_rng(seed).standard_normal drawn in the
+order Q, K, V, times the config's factor, then copied to the device.  Inputs
+(268 MB) are larger than the 126 MB L2, so no flush is needed between steps.
 
 Multi-GPU: launched by torchrun, one process per GPU over NCCL.  The (batch,
-head) slices are independent, so every rank runs its own full config-2 batch
-(weak scaling) with no data-path collective; the barrier and the max-over-ranks
-of the CUDA-event times are the only communication.
+head) slices are independent, so the FIXED workload is divided into
+contiguous slice ranges, one per rank (strong scaling: 32/N heads per GPU for
+config 2), with no data-path collective; the barrier and the max-over-ranks
+of the CUDA-event times are the only communication.  Config 5 (one slice)
+splits its keys over the ranks instead (fa_b200.kvsplit).
+
+The line also carries: `parity` (rows of the timed output against the CPU
+oracle), `precision_3xtf32` (the same workload in the library's default,
+error-compensated mode), `e2e` (the crate-API host-slice call on ordinary
+pageable buffers; pinned buffers as a sub-field), `roofline` and
+`cpu_baseline`.
 
 `--impl reference` times the CPU implementation of the same path (the C
 restatement of the crate's v2 forward; the crate itself cannot be built here)
@@ -280,13 +289,14 @@ def run_kv_split(args, cfg, rank, world, local, dev):
         dist.init_process_group("nccl", init_method="tcp://127.0.0.1:29533", rank=0,
                                 world_size=1, device_id=dev)
     bh, sq, sk, d, causal, seed, factor, _ = cfg
-    gen = torch.Generator(device=dev)
-    gen.manual_seed(seed)
-    q = torch.randn(1, sq, d, device=dev, generator=gen) * factor
+    hq, hk, hv = seeded_inputs(cfg)
+    q = torch.from_numpy(hq).to(dev).view(1, sq, d)
     k_meta = torch.empty(1, sk, d, device="meta")
     chunks = zigzag_chunks(sk, world, rank)
-    kc = [torch.randn(1, c.stop - c.start, d, device=dev, generator=gen) * factor for c in chunks]
-    vc = [torch.randn(1, c.stop - c.start, d, device=dev, generator=gen) * factor for c in chunks]
+    kc = [torch.from_numpy(hk[c.start * d:c.stop * d]).to(dev).view(1, c.stop - c.start, d)
+          for c in chunks]
+    vc = [torch.from_numpy(hv[c.start * d:c.stop * d]).to(dev).view(1, c.stop - c.start, d)
+          for c in chunks]
 
     def step():
         return kv_split_forward(q, k_meta, k_meta, causal, k_chunks=kc, v_chunks=vc)
@@ -372,8 +382,9 @@ def run_backward(args, cfg, q, k, v, out, lse, gen, rank, world, local, dev):
     import torch.distributed as dist
     import fa_b200
     bh, sq, sk, d, causal, seed, factor, _ = cfg
+    nh = q.shape[0]  # this rank's slices of the fixed workload
     steps = args.steps if args.steps <= 200 else 40
-    dout = torch.randn(bh, sq, d, device=dev, generator=gen) * factor
+    dout = torch.randn(nh, sq, d, device=dev, generator=gen) * factor
     dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
     stream = torch.cuda.current_stream()
     fa_b200.forward_device(q, k, v, out, lse, causal=causal, stream=stream)
@@ -405,9 +416,9 @@ def run_backward(args, cfg, q, k, v, out, lse, gen, rank, world, local, dev):
     step_ms = float(t.item())
     fl = 2.5 * flops_of(bh, sq, sk, d, causal)
     if rank == 0:
-        line = {"metric": "attention backward TFLOP/s", "value": world * fl / step_ms / 1e9,
+        line = {"metric": "attention backward TFLOP/s", "value": fl / step_ms / 1e9,
                 "unit": "TFLOP/s", "n_gpus": world, "steps": steps, "warmup": args.warmup,
-                "ms_per_step": step_ms, "higher_is_better": True, "scaling": "weak",
+                "ms_per_step": step_ms, "higher_is_better": True, "scaling": "strong",
                 "vs_baseline": None, "dtype": "f32", "data": "synthetic",
                 "config": dict(config_dict(args, cfg, world), precision="f32 (CUDA cores)"),
                 "clocks": clk.summary(wall0, wall1), "gpu_launches": launches,
@@ -417,14 +428,88 @@ def run_backward(args, cfg, q, k, v, out, lse, gen, rank, world, local, dev):
         dist.destroy_process_group()
 
 
-def config_dict(args, cfg, world):
+def config_dict(args, cfg, world, h0=None, h1=None):
     bh, sq, sk, d, causal, seed, factor, desc = cfg
-    return {"workload": f"{args.config}: {desc}", "batch_heads_per_gpu": bh, "seq_len_q": sq,
-            "seq_len_k": sk, "d_head": d, "causal": causal, "seed": seed,
-            "input_scale": factor, "precision": args.precision,
-            "parallelism": f"dp{world} ((batch, head) slices per GPU, no collective)",
+    per = f"{h1 - h0}" if h0 is not None else f"{bh}/{world}"
+    return {"workload": f"{args.config}: {desc}", "batch_heads": bh,
+            "batch_heads_per_gpu": per, "seq_len_q": sq, "seq_len_k": sk, "d_head": d,
+            "causal": causal, "seed": seed, "input_scale": factor,
+            "generator": "numpy default_rng(seed).standard_normal, Q then K then V, x factor",
+            "precision": args.precision,
+            "parallelism": f"dp{world} (contiguous (batch, head) slice ranges of the fixed "
+                           "workload per GPU, no collective)",
             "l2": "inputs larger than L2 (no flush)" if bytes_of(bh, sq, sk, d) > 126e6
             else "L2 flushed between steps (256 MB write)"}
+
+
+def shard_range(bh, world, rank):
+    """Contiguous (batch, head) slice range [h0, h1) of `rank` out of `world`."""
+    return bh * rank // world, bh * (rank + 1) // world
+
+
+def seeded_inputs(cfg, h0=0, h1=None):
+    """Q, K, V of a config as flat float32 arrays, slices [h0, h1) only: the
+    whole config is drawn from BASELINE's generator (so every rank sees the same
+    numbers) and this rank's slices are cut out."""
+    import numpy as np
+    bh, sq, sk, d, causal, seed, factor, _ = cfg
+    h1 = bh if h1 is None else h1
+    rng = np.random.default_rng(seed)
+    out = []
+    for n in (sq, sk, sk):
+        a = rng.standard_normal(bh * n * d, dtype=np.float32) * np.float32(factor)
+        out.append(np.ascontiguousarray(a[h0 * n * d:h1 * n * d]))
+    return out
+
+
+def parity_items(nh, sq, block=64):
+    """(head, 64-row query block) items of the oracle spread over nh slices:
+    first, middle and last blocks of the first and last slice."""
+    nb = (sq + block - 1) // block
+    pick = sorted({0, nb // 2, nb - 1})
+    return sorted({h * nb + b for h in {0, nh - 1} for b in pick})
+
+
+def parity_check(q, k, v, out, lse, nh, sq, sk, d, causal, tol, h0=0):
+    """Max abs error of sampled output rows and their LSE against the oracle
+    (the crate's v2 forward restated in C), on whole query blocks of run_v2."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import numpy as np
+    import oracle as O
+    items = parity_items(nh, sq)
+    want, wlse = O.flash_v2_items(q, k, v, nh, sq, sk, d, causal, items)
+    rows = O.item_rows(items, sq)
+    err = float(np.max(np.abs(out.reshape(-1, d)[rows].astype(np.float64) -
+                              want.reshape(-1, d)[rows])))
+    lerr = float(np.max(np.abs(lse[rows].astype(np.float64) - wlse[rows])))
+    return {"max_abs_err": err, "lse_max_abs_err": lerr, "tol": tol,
+            "pass": bool(err <= tol and lerr <= tol), "rows_checked": int(len(rows)),
+            "oracle": "oracle/fa_oracle.c (crate v2 forward restated), whole 64-row query "
+                      f"blocks {items} of slices [{h0}, {h0 + nh})"}
+
+
+def time_device(fa_b200, step, steps, stream, world):
+    """Device time per step (CUDA events on the launching stream; max over
+    ranks), and kernels launched per step."""
+    import torch
+    import torch.distributed as dist
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    launches0 = fa_b200.launch_count()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(steps):
+        step()
+    t1.record(stream)
+    torch.cuda.synchronize()
+    launches = fa_b200.launch_count() - launches0
+    fa_b200.sync_status(stream)
+    t = torch.tensor([t0.elapsed_time(t1) / steps], device="cuda", dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item()), launches
 
 
 def main():
@@ -437,6 +522,8 @@ def main():
     ap.add_argument("--precision", default="tf32", choices=sorted(PRECISION_NAMES))
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip the parity check, the 3xTF32 leg and the e2e legs (profiling)")
     ap.add_argument("--ref-budget", type=float, default=8.0)
     ap.add_argument("--kv-split", action="store_true",
                     help="config 5 through the key-range split even on one GPU")
@@ -467,18 +554,21 @@ def main():
     if args.config == "c5" and (world > 1 or args.kv_split):
         return run_kv_split(args, cfg, rank, world, local, dev)
 
-    # inputs of this rank's slices: the config's generator, offset per rank
-    gen = torch.Generator(device=dev)
-    gen.manual_seed(seed * 1000 + rank)
-    q = torch.randn(bh, sq, d, device=dev, generator=gen) * factor
-    k = torch.randn(bh, sk, d, device=dev, generator=gen) * factor
-    v = torch.randn(bh, sk, d, device=dev, generator=gen) * factor
+    # this rank's contiguous slice range of the fixed workload
+    h0, h1 = shard_range(bh, world, rank)
+    nh = h1 - h0
+    hq, hk, hv = seeded_inputs(cfg, h0, h1)
+    q = torch.from_numpy(hq).to(dev).view(nh, sq, d)
+    k = torch.from_numpy(hk).to(dev).view(nh, sk, d)
+    v = torch.from_numpy(hv).to(dev).view(nh, sk, d)
     out = torch.empty_like(q)
-    lse = torch.empty(bh, sq, device=dev)
+    lse = torch.empty(nh, sq, device=dev)
     if args.backward:
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(seed * 1000 + rank)
         return run_backward(args, cfg, q, k, v, out, lse, gen, rank, world, local, dev)
     flush = None
-    if bytes_of(bh, sq, sk, d) <= 126e6:
+    if bytes_of(nh, sq, sk, d) <= 126e6:
         flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)
     stream = torch.cuda.current_stream()
 
@@ -494,7 +584,6 @@ def main():
     fa_b200.sync_status(stream)
 
     # device-timed region: every launch of the step on `stream`
-    kernel_ms = []
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
           for _ in range(args.steps)]
     if world > 1:
@@ -527,52 +616,78 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         dist.barrier()
     step_ms = float(t.item())
-    fl = flops_of(bh, sq, sk, d, causal)
-    value = world * fl / (step_ms * 1e-3) / 1e12
+    fl_all = flops_of(bh, sq, sk, d, causal)   # the whole job (all ranks)
+    fl_rank = flops_of(nh, sq, sk, d, causal)  # this rank's share
+    value = fl_all / (step_ms * 1e-3) / 1e12
     clocks = clk.summary(wall0, wall1)
+    tol_main = 2e-3 if args.precision == "tf32" else 2e-5
 
-    # end-to-end through the public host-slice API (pinned host buffers,
-    # H2D of Q/K/V and D2H of OUT inside the timed region, every step)
-    hq = torch.empty(bh * sq * d, dtype=torch.float32, pin_memory=True)
-    hk = torch.empty(bh * sk * d, dtype=torch.float32, pin_memory=True)
-    hv = torch.empty(bh * sk * d, dtype=torch.float32, pin_memory=True)
-    ho = torch.empty(bh * sq * d, dtype=torch.float32, pin_memory=True)
-    hq.copy_(q.view(-1))
-    hk.copy_(k.view(-1))
-    hv.copy_(v.view(-1))
-    nq, nk, nv, no = hq.numpy(), hk.numpy(), hv.numpy(), ho.numpy()
-    cfgc = fa_b200.FlashAttentionConfig(64, 128, causal)
-    fa_b200.flash_attention_multihead_v2(nq, nk, nv, 1, bh, sq, sk, d, cfgc, no)
-    if world > 1:
-        dist.barrier()
-    t0 = time.perf_counter()
-    for _ in range(args.e2e_steps):
-        fa_b200.flash_attention_multihead_v2(nq, nk, nv, 1, bh, sq, sk, d, cfgc, no)
-    e2e_s = (time.perf_counter() - t0) / args.e2e_steps
-    te = torch.tensor([e2e_s], device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    e2e_s = float(te.item())
-    # the same call with ordinary pageable buffers (what a caller of the crate
-    # API passes); the library streams them through its pinned rings
-    pq, pk, pv, po = (np.array(x) for x in (nq, nk, nv, no))
-    fa_b200.flash_attention_multihead_v2(pq, pk, pv, 1, bh, sq, sk, d, cfgc, po)
-    if world > 1:
-        dist.barrier()
-    t0 = time.perf_counter()
-    for _ in range(args.e2e_steps):
-        fa_b200.flash_attention_multihead_v2(pq, pk, pv, 1, bh, sq, sk, d, cfgc, po)
-    pg_s = (time.perf_counter() - t0) / args.e2e_steps
-    te = torch.tensor([pg_s], device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    pg_s = float(te.item())
-    e2e = {"value": world * fl / e2e_s / 1e12, "unit": "TFLOP/s",
-           "h2d_bytes_per_step": 4 * (bh * sq * d + 2 * bh * sk * d),
-           "d2h_bytes_per_step": 4 * bh * sq * d, "ms_per_step": e2e_s * 1e3,
-           "api": "fa_flash_attention_multihead_v2 (host slices, synchronous)",
-           "pageable": {"value": world * fl / pg_s / 1e12, "ms_per_step": pg_s * 1e3,
-                        "note": "same call on pageable numpy buffers"}}
+    parity = None
+    extra = {}
+    if not args.no_extras:
+        # parity of the timed output (its last step) against the oracle
+        o_h = out.cpu().numpy().ravel()
+        l_h = lse.cpu().numpy().ravel()
+        if not path.startswith(("tcgen05", "simt")):
+            tol_main = 2e-5  # the exact-f32 decode path
+        parity = parity_check(hq, hk, hv, o_h, l_h, nh, sq, sk, d, causal, tol_main, h0)
+        # the library's default precision (error-compensated 3xTF32) on the same inputs
+        if args.precision == "tf32" and path.startswith("tcgen05"):
+            fa_b200.set_precision(fa_b200.PREC_3XTF32)
+            for _ in range(3):
+                step()
+            steps3 = max(20, min(args.steps // 3, 2000))
+            ms3, l3 = time_device(fa_b200, step, steps3, stream, world)
+            path3 = fa_b200.last_path()
+            p3 = parity_check(hq, hk, hv, out.cpu().numpy().ravel(), lse.cpu().numpy().ravel(),
+                              nh, sq, sk, d, causal, 2e-5, h0)
+            fa_b200.set_precision(PRECISION_NAMES[args.precision])
+            v3 = fl_all / (ms3 * 1e-3) / 1e12
+            extra["precision_3xtf32"] = {
+                "value": v3, "unit": "TFLOP/s", "ms_per_step": ms3, "steps": steps3,
+                "kernel": path3, "launches_per_step": l3 / steps3,
+                "note": "attention TFLOP/s; the tensor pipe executes 3x these FLOPs "
+                        "(hi*hi + hi*lo + lo*hi)",
+                "parity": p3}
+
+    # end-to-end through the crate API (host slices, synchronous): the call a
+    # crate user makes, on this rank's slices; copies inside the timed region
+    e2e = None
+    if not args.no_extras:
+        cfgc = fa_b200.FlashAttentionConfig(64, 128, causal)
+        po = np.empty(nh * sq * d, np.float32)
+
+        def timed_call(qa, ka, va, oa):
+            fa_b200.flash_attention_multihead_v2(qa, ka, va, 1, nh, sq, sk, d, cfgc, oa)
+            if world > 1:
+                dist.barrier()
+            t0 = time.perf_counter()
+            for _ in range(args.e2e_steps):
+                fa_b200.flash_attention_multihead_v2(qa, ka, va, 1, nh, sq, sk, d, cfgc, oa)
+            te = torch.tensor([(time.perf_counter() - t0) / args.e2e_steps], device=dev,
+                              dtype=torch.float64)
+            if world > 1:
+                dist.all_reduce(te, op=dist.ReduceOp.MAX)
+            return float(te.item())
+
+        # ordinary pageable buffers: what a caller of the crate API passes
+        pg_s = timed_call(hq, hk, hv, po)
+        # pinned buffers (fa_pin_host): the host-link floor
+        pq = torch.empty(nh * sq * d, dtype=torch.float32, pin_memory=True)
+        pk = torch.empty(nh * sk * d, dtype=torch.float32, pin_memory=True)
+        pv = torch.empty(nh * sk * d, dtype=torch.float32, pin_memory=True)
+        pout = torch.empty(nh * sq * d, dtype=torch.float32, pin_memory=True)
+        pq.numpy()[:] = hq
+        pk.numpy()[:] = hk
+        pv.numpy()[:] = hv
+        pin_s = timed_call(pq.numpy(), pk.numpy(), pv.numpy(), pout.numpy())
+        e2e = {"value": fl_all / pg_s / 1e12, "unit": "TFLOP/s",
+               "h2d_bytes_per_step": 4 * (bh * sq * d + 2 * bh * sk * d),
+               "d2h_bytes_per_step": 4 * bh * sq * d, "ms_per_step": pg_s * 1e3,
+               "api": "fa_flash_attention_multihead_v2 (host slices, synchronous) on "
+                      "pageable numpy buffers, each rank its slice range",
+               "pinned": {"value": fl_all / pin_s / 1e12, "ms_per_step": pin_s * 1e3,
+                          "note": "same call on page-locked host buffers"}}
 
     if rank != 0:
         if world > 1:
@@ -582,31 +697,36 @@ def main():
     peaks = measured_peaks()
     if path.startswith("decode"):
         bound, unit = "hbm", "GB/s"
-        achieved = bytes_of(bh, sq, sk, d) / (step_ms * 1e-3) / 1e9
+        achieved = bytes_of(nh, sq, sk, d) / (step_ms * 1e-3) / 1e9
         peak = peaks["hbm_gbs"] if peaks else 6650.0
-        peak_src = "measured hbm_gbs" if peaks else "fallback 6.65 TB/s"
+        peak_src = "measured hbm_gbs (of measured)" if peaks else "fallback 6.65 TB/s (of fallback)"
     else:
         bound, unit = "tensor", "TFLOP/s"
-        achieved = fl / (step_ms * 1e-3) / 1e12
+        achieved = fl_rank / (step_ms * 1e-3) / 1e12
         peak, peak_src = tensor_peak(peaks, step_ms * args.steps * 1e-3)
     traffic = None
     try:
         with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
             tr = json.load(f).get(f"{args.config}/{args.precision}")
-            if tr:
+            if tr and world == 1:
                 traffic = tr["bytes_per_launch"]
     except OSError:
         pass
     roof = {"bound": bound, "achieved": achieved, "peak": peak, "unit": unit,
             "frac": achieved / peak, "traffic": traffic, "peak_source": peak_src,
-            "kernel": path, "launches_per_step": launches / args.steps}
+            "kernel": path, "launches_per_step": launches / args.steps,
+            "per": "rank 0's launch (its slice range), device time"}
     line = {"metric": "attention TFLOP/s", "value": value, "unit": "TFLOP/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None,
             "dtype": "tf32" if args.precision == "tf32" and not path.startswith(("decode", "simt"))
             else ("3xtf32" if args.precision == "3xtf32" and path.startswith("tcgen05") else "f32"),
-            "data": "synthetic", "config": config_dict(args, cfg, world),
-            "clocks": clocks, "e2e": e2e, "gpu_launches": launches, "roofline": roof}
+            "data": "synthetic (BASELINE generator)",
+            "config": config_dict(args, cfg, world, h0, h1),
+            "clocks": clocks, "e2e": e2e, "gpu_launches": launches, "roofline": roof,
+            "parity": parity}
+    line.update(extra)
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(cfg)
     print(json.dumps(line), flush=True)

@@ -3,6 +3,7 @@
 // selection, and the error side channel.  Every compute step is a kernel of
 // this library; there is no CPU path.
 #include "fa_common.cuh"
+#include "fa_host.h"
 #include "../../include/fa_b200.h"
 
 #include <atomic>
@@ -65,23 +66,17 @@ int precision() {
   return p;
 }
 
-// Make the library's device current and initialise its state once.
-int prepare_device(int* dev_out) {
+// Make `dev` current and initialise the library's state on it once.
+int prepare_device_at(int dev) {
   int n = 0;
   cudaError_t e = cudaGetDeviceCount(&n);
   if (e != cudaSuccess || n == 0) {
     cudaGetLastError();
     return set_err(FA_ERR_NO_DEVICE, "no CUDA device available (this library has no CPU path)");
   }
-  int dev = g_device.load();
-  if (dev < 0) {
-    e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return cuda_err(e, "cudaGetDevice");
-  } else {
-    e = cudaSetDevice(dev);
-    if (e != cudaSuccess) return cuda_err(e, "cudaSetDevice");
-  }
-  if (dev >= kMaxDevices) return set_err(FA_ERR_ARG, "device index too large");
+  if (dev < 0 || dev >= n || dev >= kMaxDevices) return set_err(FA_ERR_ARG, "device index out of range");
+  e = cudaSetDevice(dev);
+  if (e != cudaSuccess) return cuda_err(e, "cudaSetDevice");
   DeviceState& st = g_dev[dev];
   std::call_once(st.once, [&] {
     cudaDeviceProp prop;
@@ -104,8 +99,65 @@ int prepare_device(int* dev_out) {
   if (st.init_err != cudaSuccess) return cuda_err(st.init_err, "device initialisation");
   if (st.cc_major != 10)
     return set_err(FA_ERR_NO_DEVICE, "this library is built for sm_100a (B200) only");
+  return FA_OK;
+}
+
+// The library's device (fa_set_device, else the CUDA current device), made
+// current and initialised.
+int prepare_device(int* dev_out) {
+  int dev = g_device.load();
+  if (dev < 0) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) {
+      cudaGetLastError();
+      return set_err(FA_ERR_NO_DEVICE, "no CUDA device available (this library has no CPU path)");
+    }
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_err(e, "cudaGetDevice");
+  }
+  int rc = prepare_device_at(dev);
+  if (rc) return rc;
   *dev_out = dev;
   return FA_OK;
+}
+
+// Devices of the host-slice calls (fa_set_devices / FA_B200_DEVICES).  An
+// empty list means the single device of prepare_device().
+std::mutex g_devs_m;
+bool g_devs_read = false;
+std::vector<int> g_devs;
+
+void read_devices_env() {  // under g_devs_m
+  if (g_devs_read) return;
+  g_devs_read = true;
+  const char* s = std::getenv("FA_B200_DEVICES");
+  if (!s || !*s) return;
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess) {
+    cudaGetLastError();
+    return;
+  }
+  std::vector<int> v;
+  if (!strcmp(s, "all")) {
+    for (int i = 0; i < n && i < kMaxDevices; i++) v.push_back(i);
+  } else {
+    const char* c = s;
+    while (*c) {
+      char* end = nullptr;
+      long x = strtol(c, &end, 10);
+      if (end == c || x < 0 || x >= n || v.size() >= (size_t)kMaxDevices) return;  // ignored
+      v.push_back((int)x);
+      c = *end == ',' ? end + 1 : end;
+      if (*end && *end != ',') return;
+    }
+  }
+  if (v.size() > 1) g_devs = v;
+}
+
+std::vector<int> device_list() {
+  std::lock_guard<std::mutex> lk(g_devs_m);
+  read_devices_env();
+  return g_devs;
 }
 
 bool mul_ok(size_t a, size_t b, size_t* r) {
@@ -354,13 +406,10 @@ int host_forward_staged(const float* q, const float* k, const float* v, size_t b
   return rc;
 }
 
-// Host-slice forward: stage to HBM, run, copy back, check.
-int host_forward(const float* q, const float* k, const float* v, size_t bh, size_t sq,
-                 size_t sk, size_t d, int causal, float* out, float* lse) {
-  if (bh > (size_t)INT32_MAX || sq > (size_t)INT32_MAX || sk > (size_t)INT32_MAX || d > 256)
-    return set_err(d > 256 ? FA_ERR_UNSUPPORTED : FA_ERR_ARG, "dimension too large");
-  int dev = 0;
-  int rc = prepare_device(&dev);
+// Host-slice forward on one device: stage to HBM, run, copy back, check.
+int host_forward_one(int dev, const float* q, const float* k, const float* v, size_t bh,
+                     size_t sq, size_t sk, size_t d, int causal, float* out, float* lse) {
+  int rc = prepare_device_at(dev);
   if (rc) return rc;
   cudaStream_t* st;
   if ((rc = host_streams(dev, &st))) return rc;
@@ -446,6 +495,21 @@ int host_forward(const float* q, const float* k, const float* v, size_t bh, size
   return rc;
 }
 
+// Host-slice forward: the device list (several GPUs), else one device.
+int host_forward(const float* q, const float* k, const float* v, size_t bh, size_t sq,
+                 size_t sk, size_t d, int causal, float* out, float* lse) {
+  if (bh > (size_t)INT32_MAX || sq > (size_t)INT32_MAX || sk > (size_t)INT32_MAX || d > 256)
+    return set_err(d > 256 ? FA_ERR_UNSUPPORTED : FA_ERR_ARG, "dimension too large");
+  const std::vector<int> devs = device_list();
+  if (devs.size() > 1)
+    return fa::host_forward_devices(devs.data(), (int)devs.size(), q, k, v, bh, sq, sk, d, causal,
+                                    out, lse);
+  int dev = 0;
+  int rc = prepare_device(&dev);
+  if (rc) return rc;
+  return host_forward_one(dev, q, k, v, bh, sq, sk, d, causal, out, lse);
+}
+
 int single_head(const float* q, size_t q_len, const float* k, size_t k_len, const float* v,
                 size_t v_len, size_t sq, size_t sk, size_t d, const fa_config* cfg, float* out,
                 size_t out_len) {
@@ -503,6 +567,21 @@ int device_forward(const float* q, const float* k, const float* v, float* out, f
 }
 
 }  // namespace
+
+// Internal interface of the multi-device orchestration (fa_host.h).
+namespace fa {
+int status_error(int code, const std::string& msg) { return set_err(code, msg); }
+int status_cuda(cudaError_t e, const char* what) { return cuda_err(e, what); }
+std::string status_message() { return t_err; }
+int prepare_device_on(int dev) { return prepare_device_at(dev); }
+int device_sm_count(int dev) { return g_dev[dev].num_sms; }
+int dispatch_on(FwdParams p, int dev, cudaStream_t s) { return dispatch(p, dev, s); }
+int check_err_flag_on(int dev, cudaStream_t s) { return check_err_flag(dev, s); }
+int host_forward_on(int dev, const float* q, const float* k, const float* v, size_t bh,
+                    size_t sq, size_t sk, size_t d, int causal, float* out, float* lse) {
+  return host_forward_one(dev, q, k, v, bh, sq, sk, d, causal, out, lse);
+}
+}  // namespace fa
 
 extern "C" {
 
@@ -741,6 +820,32 @@ int fa_set_device(int device) {
   return FA_OK;
 }
 
+int fa_set_devices(const int* devices, int n) {
+  t_err.clear();
+  if (n < 0 || n > kMaxDevices || (n > 0 && !devices))
+    return set_err(FA_ERR_ARG, "device list: bad pointer or length");
+  int count = 0;
+  if (n > 0 && (cudaGetDeviceCount(&count) != cudaSuccess || count == 0)) {
+    cudaGetLastError();
+    return set_err(FA_ERR_NO_DEVICE, "no CUDA device available");
+  }
+  for (int i = 0; i < n; i++)
+    if (devices[i] < 0 || devices[i] >= count) return set_err(FA_ERR_ARG, "device index out of range");
+  std::lock_guard<std::mutex> lk(g_devs_m);
+  g_devs_read = true;  // an explicit list overrides FA_B200_DEVICES
+  g_devs.clear();
+  if (n > 1) g_devs.assign(devices, devices + n);
+  else if (n == 1) g_device.store(devices[0]);
+  return FA_OK;
+}
+
+int fa_get_devices(int* devices, int capacity) {
+  const std::vector<int> v = device_list();
+  if (devices)
+    for (int i = 0; i < (int)v.size() && i < capacity; i++) devices[i] = v[i];
+  return (int)v.size();
+}
+
 int fa_device_count(void) {
   int n = 0;
   if (cudaGetDeviceCount(&n) != cudaSuccess) {
@@ -784,6 +889,7 @@ void fa_shutdown(void) {
   int cur = 0;
   const bool have_cur = cudaGetDevice(&cur) == cudaSuccess;
   fa::staging_release_all();
+  fa::devices_release();
   // the calling thread's streams, pipeline events and pinned error word
   for (int d = 0; d < kMaxDevices; d++) {
     bool set = false;

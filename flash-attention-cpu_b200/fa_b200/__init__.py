@@ -36,7 +36,7 @@ __all__ = [
     "flash_attention_multihead_v3", "flash_attention_multihead",
     "multihead_lse", "forward_device", "forward_decode_noalloc", "forward_partial_device", "lse_combine_device",
     "set_precision", "get_precision", "launch_count", "last_path", "sync_status",
-    "device_count", "lib_path", "PREC_TF32", "PREC_3XTF32", "PREC_FP32",
+    "device_count", "set_device", "set_devices", "get_devices", "lib_path", "PREC_TF32", "PREC_3XTF32", "PREC_FP32",
 ]
 
 PREC_TF32, PREC_3XTF32, PREC_FP32 = 0, 1, 2
@@ -120,6 +120,10 @@ def _load():
     L.fa_set_device.argtypes = [ctypes.c_int]
     L.fa_set_device.restype = ctypes.c_int
     L.fa_device_count.restype = ctypes.c_int
+    L.fa_set_devices.argtypes = [ctypes.POINTER(ctypes.c_int), ctypes.c_int]
+    L.fa_set_devices.restype = ctypes.c_int
+    L.fa_get_devices.argtypes = [ctypes.POINTER(ctypes.c_int), ctypes.c_int]
+    L.fa_get_devices.restype = ctypes.c_int
     L.fa_last_error.restype = ctypes.c_char_p
     L.fa_last_path.restype = ctypes.c_char_p
     L.fa_launch_count.restype = ctypes.c_uint64
@@ -299,6 +303,22 @@ def get_precision() -> int:
 
 def set_device(dev: int) -> None:
     _check(_load().fa_set_device(int(dev)))
+
+
+def set_devices(devices) -> None:
+    """Devices the host-slice calls spread over (fa_set_devices): a list of
+    device indices (repeats allowed), [] for one device."""
+    devs = [int(x) for x in devices]
+    arr = (ctypes.c_int * max(1, len(devs)))(*devs)
+    _check(_load().fa_set_devices(arr, len(devs)))
+
+
+def get_devices() -> list:
+    L = _load()
+    n = L.fa_get_devices(None, 0)
+    arr = (ctypes.c_int * max(1, n))()
+    L.fa_get_devices(arr, n)
+    return [arr[i] for i in range(n)]
 
 
 def device_count() -> int:

@@ -209,6 +209,24 @@ FA_API int fa_set_precision(int precision); /* fa_precision */
 FA_API int fa_get_precision(void);
 /* Device used by the host-slice calls (default: the CUDA current device). */
 FA_API int fa_set_device(int device);
+/* Devices the host-slice calls (fa_flash_attention*, _multihead*, _lse) spread
+ * over, one process driving them all.  The crate fans its (batch, head) slices
+ * out over every core (src/common.rs:72-101); with n > 1 devices these calls
+ * give each device a contiguous range of slices (its own copies over its own
+ * host link, its own kernels; no collective), and a call with fewer slices
+ * than devices on long sequences (seq_len_q > 16, seq_len_k >= 2048 per
+ * device, seq_len_q*seq_len_k*d_head >= 8e9: the crate's single-head
+ * flash_attention_v2 on a long head, src/v2.rs:49-121) splits each slice's
+ * keys over the devices and merges the partial outputs by log-sum-exp after
+ * peer copies of the partials.  Results equal the one-device results to
+ * within the precision mode's tolerance.  A device may be listed more than
+ * once (its entries then share that GPU).  n == 1 is fa_set_device(devices[0]);
+ * n == 0 returns to one device.  Overrides FA_B200_DEVICES ("0,1,2,3" or
+ * "all", read at first use).  The device-resident calls are unaffected. */
+FA_API int fa_set_devices(const int* devices, int n);
+/* Copies up to `capacity` entries of the device list into `devices` and
+ * returns its length (0: one device, see fa_set_device). */
+FA_API int fa_get_devices(int* devices, int capacity);
 FA_API int fa_device_count(void);
 /* Thread-local message of the last failure on this thread ("" if none). */
 FA_API const char* fa_last_error(void);

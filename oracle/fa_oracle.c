@@ -225,6 +225,7 @@ typedef struct {
   size_t bh, sq, sk, d, br, bc;
   int causal;
   size_t nq, next, limit;
+  const size_t *items; /* nullable: explicit (head * nq + block) item list */
   pthread_mutex_t mu;
 } mh_job;
 
@@ -238,6 +239,7 @@ static void *mh_worker(void *arg) {
     size_t item = J->next++;
     pthread_mutex_unlock(&J->mu);
     if (item >= J->limit) break;
+    if (J->items) item = J->items[item];
     size_t h = item / J->nq, qi = item % J->nq;
     v2_query_block(J->q + h * J->sq * J->d, J->k + h * J->sk * J->d,
                    J->v + h * J->sk * J->d, J->sq, J->sk, J->d, J->br, J->bc,
@@ -248,14 +250,11 @@ static void *mh_worker(void *arg) {
   return NULL;
 }
 
-/* Multihead v2 over bh = batch*heads contiguous [sq,d] / [sk,d] slices.
- * max_items bounds the work (0 = all (head, query block) items); the first
- * max_items items in head-major order are computed.  Returns items done. */
-long oracle_flash_v2_multihead(const float *q, const float *k, const float *v,
-                               size_t bh, size_t sq, size_t sk, size_t d,
-                               size_t block_q, size_t block_kv, int causal,
-                               float *out, float *lse, int nthreads,
-                               size_t max_items) {
+static long run_items(const float *q, const float *k, const float *v, size_t bh,
+                      size_t sq, size_t sk, size_t d, size_t block_q,
+                      size_t block_kv, int causal, float *out, float *lse,
+                      int nthreads, size_t max_items, const size_t *items,
+                      size_t n_items) {
   if (bh == 0 || sq == 0 || sk == 0 || d == 0) return 0;
   mh_job J;
   J.q = q; J.k = k; J.v = v; J.out = out; J.lse = lse;
@@ -264,8 +263,15 @@ long oracle_flash_v2_multihead(const float *q, const float *k, const float *v,
   J.causal = causal;
   J.nq = (sq + J.br - 1) / J.br;
   J.next = 0;
-  J.limit = bh * J.nq;
-  if (max_items && max_items < J.limit) J.limit = max_items;
+  J.items = items;
+  if (items) {
+    for (size_t i = 0; i < n_items; i++)
+      if (items[i] >= bh * J.nq) return -1;
+    J.limit = n_items;
+  } else {
+    J.limit = bh * J.nq;
+    if (max_items && max_items < J.limit) J.limit = max_items;
+  }
   pthread_mutex_init(&J.mu, NULL);
   if (nthreads < 1) nthreads = 1;
   if (nthreads > 512) nthreads = 512;
@@ -274,6 +280,31 @@ long oracle_flash_v2_multihead(const float *q, const float *k, const float *v,
   for (int t = 0; t < nthreads; t++) pthread_join(th[t], NULL);
   pthread_mutex_destroy(&J.mu);
   return (long)J.limit;
+}
+
+/* Multihead v2 over bh = batch*heads contiguous [sq,d] / [sk,d] slices.
+ * max_items bounds the work (0 = all (head, query block) items); the first
+ * max_items items in head-major order are computed.  Returns items done. */
+long oracle_flash_v2_multihead(const float *q, const float *k, const float *v,
+                               size_t bh, size_t sq, size_t sk, size_t d,
+                               size_t block_q, size_t block_kv, int causal,
+                               float *out, float *lse, int nthreads,
+                               size_t max_items) {
+  return run_items(q, k, v, bh, sq, sk, d, block_q, block_kv, causal, out, lse,
+                   nthreads, max_items, NULL, 0);
+}
+
+/* The same forward for the listed items only: item = head * n_blocks + block,
+ * n_blocks = ceil(sq / block_q).  Each item is one query block of run_v2, so
+ * its rows come out exactly as in a full run.  Returns the item count, or -1
+ * for an item out of range. */
+long oracle_flash_v2_items(const float *q, const float *k, const float *v,
+                           size_t bh, size_t sq, size_t sk, size_t d,
+                           size_t block_q, size_t block_kv, int causal,
+                           float *out, float *lse, int nthreads,
+                           const size_t *items, size_t n_items) {
+  return run_items(q, k, v, bh, sq, sk, d, block_q, block_kv, causal, out, lse,
+                   nthreads, 0, items, n_items);
 }
 
 /* naive_attention restated (naive.rs:14-75), f32, one head. */

@@ -58,6 +58,10 @@ def lib():
         L.oracle_flash_v2_multihead.restype = ctypes.c_long
         L.oracle_flash_v2_multihead.argtypes = [_F, _F, _F, _SZ, _SZ, _SZ, _SZ, _SZ, _SZ,
                                                 ctypes.c_int, _F, _F, ctypes.c_int, _SZ]
+        L.oracle_flash_v2_items.restype = ctypes.c_long
+        L.oracle_flash_v2_items.argtypes = [_F, _F, _F, _SZ, _SZ, _SZ, _SZ, _SZ, _SZ,
+                                            ctypes.c_int, _F, _F, ctypes.c_int,
+                                            ctypes.POINTER(_SZ), _SZ]
         L.oracle_naive_f32.restype = None
         L.oracle_naive_f32.argtypes = [_F, _F, _F, _SZ, _SZ, _SZ, ctypes.c_int, _F]
         L.oracle_naive_f64_rows.restype = None
@@ -103,6 +107,39 @@ def flash_v2_multihead(q, k, v, bh, sq, sk, d, causal, block_q=64, block_kv=128,
         _fp(q), _fp(k), _fp(v), bh, sq, sk, d, block_q, block_kv, int(causal),
         out.ctypes.data_as(_F), lse.ctypes.data_as(_F), int(nthreads), int(max_items))
     return out, lse[: bh * sq], items
+
+
+def flash_v2_items(q, k, v, bh, sq, sk, d, causal, items, block_q=64, block_kv=128,
+                   nthreads=None):
+    """v2 forward of the listed (head, query block) items only.
+
+    `items` are indices head * ceil(sq / block_q) + block.  Returns (out, lse)
+    as full-size arrays in which only the rows of the listed items are written
+    (out zeros, lse -inf elsewhere); each computed row equals the row a full
+    run produces.
+    """
+    q, k, v = _c32(q), _c32(k), _c32(v)
+    out = np.zeros(bh * sq * d, np.float32)
+    lse = np.full(max(bh * sq, 1), -np.inf, np.float32)
+    it = np.ascontiguousarray(np.asarray(items, dtype=np.uint64))
+    n = lib().oracle_flash_v2_items(
+        _fp(q), _fp(k), _fp(v), bh, sq, sk, d, block_q, block_kv, int(causal),
+        out.ctypes.data_as(_F), lse.ctypes.data_as(_F), int(nthreads or os.cpu_count() or 1),
+        it.ctypes.data_as(ctypes.POINTER(_SZ)), it.size)
+    if n < 0:
+        raise ValueError("item out of range")
+    return out, lse[: bh * sq]
+
+
+def item_rows(items, sq, block_q=64):
+    """Global row indices (head * sq + row) covered by the listed items."""
+    nb = (sq + block_q - 1) // block_q
+    rows = []
+    for it in items:
+        h, b = divmod(int(it), nb)
+        r0 = b * block_q
+        rows.extend(h * sq + r for r in range(r0, min(sq, r0 + block_q)))
+    return np.asarray(rows, dtype=np.int64)
 
 
 def naive_f32(q, k, v, sq, sk, d, causal):

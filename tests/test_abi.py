@@ -164,3 +164,12 @@ def test_noalloc_refuses_before_any_device_call():
                                        None) == FA_ERR_UNSUPPORTED
     assert b"seq_len_k" in L.fa_last_error()
     assert fa_b200.launch_count() == n0
+
+
+def test_device_list_control_without_a_gpu():
+    if fa_b200.device_count() > 0:
+        pytest.skip("a GPU is present")
+    fa_b200.set_devices([])  # returning to one device needs no GPU
+    assert fa_b200.get_devices() == []
+    with pytest.raises(fa_b200.FaError, match="FA_ERR_NO_DEVICE"):
+        fa_b200.set_devices([0, 1])

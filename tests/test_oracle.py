@@ -132,3 +132,21 @@ def test_partial_run_matches_full_run_on_its_rows():
     assert n_full == (sq + 63) // 64 and n_part == 2
     assert np.array_equal(part[:128 * d], full[:128 * d])
     assert np.array_equal(lp[:128], lf[:128])
+
+
+@pytest.mark.parametrize("causal", [False, True])
+def test_listed_query_blocks_equal_the_full_run(causal):
+    # oracle_flash_v2_items computes single query blocks of run_v2 (used to
+    # check a 131072-row head on sampled blocks): each listed block's rows must
+    # be bit-identical to the same rows of a full multihead run.
+    bh, sq, sk, d = 3, 300, 200, 64
+    q, k, v = random_vec(bh * sq * d, 5), random_vec(bh * sk * d, 6), random_vec(bh * sk * d, 7)
+    full, flse, _ = O.flash_v2_multihead(q, k, v, bh, sq, sk, d, causal)
+    items = [0, 4, 7, 14]
+    part, plse = O.flash_v2_items(q, k, v, bh, sq, sk, d, causal, items)
+    rows = O.item_rows(items, sq)
+    assert len(rows) == 64 + 44 + 64 + 44
+    assert np.array_equal(full.reshape(-1, d)[rows], part.reshape(-1, d)[rows])
+    assert np.array_equal(flse[rows], plse[rows])
+    with pytest.raises(ValueError):
+        O.flash_v2_items(q, k, v, bh, sq, sk, d, causal, [15])
