@@ -30,6 +30,9 @@ thread_local const char* t_path = "";
 
 std::atomic<int> g_precision{-1};
 std::atomic<int> g_device{-1};
+// test hook (fa_test_stall): the abortable-wait limit and the withheld arrive
+std::atomic<unsigned long long> g_wait_ns{fa::kWaitLimitNs};
+std::atomic<int> g_test_skip{-1};
 
 constexpr int kMaxDevices = 64;
 struct DeviceState {
@@ -171,6 +174,8 @@ int dispatch(fa::FwdParams p, int dev, cudaStream_t s) {
   const int prec = precision();
   DeviceState& st = g_dev[dev];
   p.err = st.err_flag;
+  p.wait_ns = g_wait_ns.load();
+  p.test_skip = g_test_skip.load();
   p.scale = 1.0f / sqrtf((float)p.d);
   p.scale_log2 = p.scale * 1.4426950408889634f;
   cudaError_t e = cudaSuccess;
@@ -800,6 +805,12 @@ int fa_sync_status(void* stream) {
   int rc = prepare_device(&dev);
   if (rc) return rc;
   return check_err_flag(dev, (cudaStream_t)stream);
+}
+
+int fa_test_stall(int skip_block, unsigned long long wait_ns) {
+  g_wait_ns.store(wait_ns ? wait_ns : fa::kWaitLimitNs);
+  g_test_skip.store(skip_block < 0 ? -1 : skip_block);
+  return FA_OK;
 }
 
 int fa_set_precision(int p) {

@@ -22,6 +22,12 @@ struct FwdParams {
   float scale;       // 1/sqrt(d), computed in f32 as the crate does (v2.rs:171)
   float scale_log2;  // scale * log2(e): scores go straight into exp2
   int* err;          // device error word (0 = ok), see ErrCode
+  // Limit of the tensor-core kernels' abortable waits (kWaitLimitNs unless a
+  // test shortens it), and the test hook: with test_skip >= 0, one softmax
+  // warp of the first CTA (pair) does not announce P of key block test_skip,
+  // so the MMA issuer's wait for it runs out and the abort path is taken.
+  unsigned long long wait_ns;
+  int test_skip;
 };
 
 // Backward pass (fa_bwd.cu): gradients of the forward above.

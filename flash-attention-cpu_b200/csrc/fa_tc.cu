@@ -214,7 +214,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int sk = j % NKS;
         {
           FA_TR_T0();
-          if (j >= NKS) ok = mbar_wait(bar_k_empty(sk), ((j / NKS) & 1) ^ 1, abort_flag, p.err);
+          if (j >= NKS) ok = mbar_wait(bar_k_empty(sk), ((j / NKS) & 1) ^ 1, abort_flag, p.err, p.wait_ns);
           FA_TR_ADD(0);
         }
         if (!ok) break;
@@ -242,7 +242,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int sv = g % NVS;
         {
           FA_TR_T0();
-          if (g >= NVS) ok = mbar_wait(bar_v_empty(sv), ((g / NVS) & 1) ^ 1, abort_flag, p.err);
+          if (g >= NVS) ok = mbar_wait(bar_v_empty(sv), ((g / NVS) & 1) ^ 1, abort_flag, p.err, p.wait_ns);
           FA_TR_ADD(1);
         }
         if (!ok) break;
@@ -262,13 +262,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (!skip) {
       constexpr uint32_t idesc_qk = instr_desc(kBM, BK, false);
       constexpr uint32_t idesc_pv = instr_desc(kBM, D, true);
-      bool ok = __all_sync(0xffffffffu, mbar_wait(bar_q_full, 0, abort_flag, p.err));
+      bool ok = __all_sync(0xffffffffu, mbar_wait(bar_q_full, 0, abort_flag, p.err, p.wait_ns));
       tc_fence_after();
       auto issue_pv = [&](int jj) -> bool {
         const int b = jj & 1;
         {
           FA_TR_T0();
-          if (!__all_sync(0xffffffffu, mbar_wait(bar_p_full(b), (jj >> 1) & 1, abort_flag, p.err)))
+          if (!__all_sync(0xffffffffu, mbar_wait(bar_p_full(b), (jj >> 1) & 1, abort_flag, p.err, p.wait_ns)))
             return false;
           if (lane == 0) FA_TR_ADD(3);
         }
@@ -277,7 +277,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int g = jj * VS + h, sv = g % NVS;
           {
             FA_TR_T0();
-            if (!__all_sync(0xffffffffu, mbar_wait(bar_v_full(sv), (g / NVS) & 1, abort_flag, p.err)))
+            if (!__all_sync(0xffffffffu, mbar_wait(bar_v_full(sv), (g / NVS) & 1, abort_flag, p.err, p.wait_ns)))
               return false;
             if (lane == 0) FA_TR_ADD(4);
           }
@@ -298,7 +298,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int s = j % NKS, b = j & 1;
         {
           FA_TR_T0();
-          ok = __all_sync(0xffffffffu, mbar_wait(bar_k_full(s), (j / NKS) & 1, abort_flag, p.err));
+          ok = __all_sync(0xffffffffu, mbar_wait(bar_k_full(s), (j / NKS) & 1, abort_flag, p.err, p.wait_ns));
           if (lane == 0) FA_TR_ADD(2);
         }
         if (!ok) break;
@@ -356,7 +356,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int b = j & 1;
       {
         FA_TR_T0();
-        ok = __all_sync(0xffffffffu, mbar_wait(bar_s_full(b), (j >> 1) & 1, abort_flag, p.err));
+        ok = __all_sync(0xffffffffu, mbar_wait(bar_s_full(b), (j >> 1) & 1, abort_flag, p.err, p.wait_ns));
         if (threadIdx.x == 128) FA_TR_ADD(5);
       }
       if (!ok) break;
@@ -404,7 +404,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (__any_sync(0xffffffffu, need)) {
         if (threadIdx.x == 128) FA_TR_CNT(7);
         // O is being accumulated by PV_{j-1}: wait for it, then rescale in TMEM.
-        ok = __all_sync(0xffffffffu, mbar_wait(bar_o_done, (j - 1) & 1, abort_flag, p.err));
+        ok = __all_sync(0xffffffffu, mbar_wait(bar_o_done, (j - 1) & 1, abort_flag, p.err, p.wait_ns));
         if (!ok) break;
         tc_fence_after();
 #pragma unroll
@@ -445,7 +445,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       l += (rs[0] + rs[1]) + (rs[2] + rs[3]);
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(bar_p_full(b));
+      // (test hook: one thread of the first CTA withholds its arrive)
+      if (!(p.test_skip == j && threadIdx.x == 128 && blockIdx.x == 0 && blockIdx.y == 0 &&
+            blockIdx.z == 0))
+        mbar_arrive(bar_p_full(b));
       if (threadIdx.x == 128) {
         FA_TR_ADD(6);
         FA_TR_CNT(8);
@@ -453,7 +456,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     // epilogue: out = O / l, lse = ln(sum exp(s)) = (m + log2 l) * ln 2
     if (n_kv > 0) {
-      const bool w = ok ? mbar_wait(bar_o_final, 0, abort_flag, p.err) : false;
+      const bool w = ok ? mbar_wait(bar_o_final, 0, abort_flag, p.err, p.wait_ns) : false;
       ok = __all_sync(0xffffffffu, w);
     }
     if (ok) {
@@ -776,7 +779,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(NG), 1)
           const int s = G % NS;
           if (G >= NS)
             ok = mbar_wait(is_k ? bar_k_empty(s) : bar_v_empty(s), ((G / NS) & 1) ^ 1, abort_flag,
-                           p.err);
+                           p.err, p.wait_ns);
           if (!ok) break;
           FA_EV(is_k ? 12 : 11, G);
           const uint32_t full = at_leader(is_k ? bar_k_full(s) : bar_v_full(s));
@@ -816,10 +819,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(NG), 1)
       // PV of global block G (block j of its tile): O (+)= P(G) V(G)
       auto issue_pv = [&](int G, int j) -> bool {
         const int b = G & 1, sv = G % NVS;
-        if (!__all_sync(0xffffffffu, mbar_wait(bar_p_full(b), (G >> 1) & 1, abort_flag, p.err)))
+        if (!__all_sync(0xffffffffu, mbar_wait(bar_p_full(b), (G >> 1) & 1, abort_flag, p.err, p.wait_ns)))
           return false;
         if (lane == 0) FA_EV(2, G);
-        if (!__all_sync(0xffffffffu, mbar_wait(bar_v_full(sv), (G / NVS) & 1, abort_flag, p.err)))
+        if (!__all_sync(0xffffffffu, mbar_wait(bar_v_full(sv), (G / NVS) & 1, abort_flag, p.err, p.wait_ns)))
           return false;
         if (lane == 0) FA_EV(3, G);
         tc_fence_after();
@@ -840,13 +843,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(NG), 1)
         const int w = work_of(k);
         if (w >= n_work) continue;
         const Tile t = tile_of(w);
-        ok = __all_sync(0xffffffffu, mbar_wait(bar_q_full, it & 1, abort_flag, p.err));
+        ok = __all_sync(0xffffffffu, mbar_wait(bar_q_full, it & 1, abort_flag, p.err, p.wait_ns));
         if (!ok) break;
         tc_fence_after();
         for (int j = 0; j < t.n_kv && ok; j++) {
           const int Gj = G + j, s = Gj % NKS, b = Gj & 1;
           if (lane == 0) FA_EV(13, Gj);
-          ok = __all_sync(0xffffffffu, mbar_wait(bar_k_full(s), (Gj / NKS) & 1, abort_flag, p.err));
+          ok = __all_sync(0xffffffffu, mbar_wait(bar_k_full(s), (Gj / NKS) & 1, abort_flag, p.err, p.wait_ns));
           if (!ok) break;
           if (lane == 0) FA_EV(0, Gj);
           tc_fence_after();
@@ -908,7 +911,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(NG), 1)
       if (k0 >= 0) load_q(tile_of(work_of(k0)));
       for (int k = k0; k >= 0 && ok; k = next_work(k)) {
         const Tile t = tile_of(work_of(k));
-        ok = mbar_wait(bar_o_smem_full, it & 1, abort_flag, p.err);
+        ok = mbar_wait(bar_o_smem_full, it & 1, abort_flag, p.err, p.wait_ns);
         if (!ok) break;
         if (have_prev) store(false);
         FA_EV(18, it);
@@ -918,7 +921,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(NG), 1)
         pt = t;
         it++;
       }
-      if (ok && have_prev && mbar_wait(bar_o_smem_full, it & 1, abort_flag, p.err)) store(true);
+      if (ok && have_prev && mbar_wait(bar_o_smem_full, it & 1, abort_flag, p.err, p.wait_ns)) store(true);
       // no Q load may land after exit, even when a consumer role aborted
       volatile int no_abort = 0;
       if (qit > 0) mbar_wait(bar_q_smem_full, (qit - 1) & 1, &no_abort, p.err);
@@ -968,7 +971,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(NG), 1)
     auto epilogue_smem = [&](bool go, float* l_out) -> bool {
       // all NG warps of the quarter reach this on every path
       bool w = go;
-      if (w) w = __all_sync(0xffffffffu, mbar_wait(bar_o_final, pit & 1, abort_flag, p.err));
+      if (w) w = __all_sync(0xffffffffu, mbar_wait(bar_o_final, pit & 1, abort_flag, p.err, p.wait_ns));
       if (*abort_flag) w = false;
       // row-sum exchange slot alternates by tile, so a slot is rewritten only
       // after every warp of the quarter has passed the next epilogue's barrier
@@ -1016,7 +1019,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(NG), 1)
       // written.
       if (lane == 0 && quarter == 0 && g == 0) FA_EV(17, G);
       const bool okq =
-          ok && __all_sync(0xffffffffu, mbar_wait(bar_q_smem_full, it & 1, abort_flag, p.err));
+          ok && __all_sync(0xffffffffu, mbar_wait(bar_q_smem_full, it & 1, abort_flag, p.err, p.wait_ns));
       if (lane == 0 && quarter == 0 && g == 0) FA_EV(14, G);
       if (okq) {
 #pragma unroll
@@ -1056,7 +1059,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(NG), 1)
       for (int j = 0; j < t.n_kv && ok; j++) {
         const int Gj = G + j, b = Gj & 1;
         const bool wt =
-            __all_sync(0xffffffffu, mbar_wait(bar_s_full(b), (Gj >> 1) & 1, abort_flag, p.err));
+            __all_sync(0xffffffffu, mbar_wait(bar_s_full(b), (Gj >> 1) & 1, abort_flag, p.err, p.wait_ns));
         if (lane == 0 && quarter == 0 && g < 2) FA_EV(5 + 3 * g, Gj);
         tc_fence_after();
         float x[HC];
@@ -1118,7 +1121,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(NG), 1)
           m = m_new;
         }
         if (__any_sync(0xffffffffu, need) &&
-            __all_sync(0xffffffffu, mbar_wait(bar_o_done, (Gj - 1) & 1, abort_flag, p.err))) {
+            __all_sync(0xffffffffu, mbar_wait(bar_o_done, (Gj - 1) & 1, abort_flag, p.err, p.wait_ns))) {
           // (a failed wait raises the abort flag; the loop then ends at the
           // next block's bar_any)
           tc_fence_after();
@@ -1161,7 +1164,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(NG), 1)
 
         tmem_wait_st();
         tc_fence_before();
-        warp_arrive_leader(bar_p_full(b));
+        // (test hook: the first softmax warp of the first pair's leader
+        // withholds its arrive)
+        if (!(p.test_skip == Gj && blockIdx.x == 0 && warp == kSoftmaxWarp0))
+          warp_arrive_leader(bar_p_full(b));
         if (lane == 0 && quarter == 0 && g < 2) FA_EV(7 + 3 * g, Gj);
       }
       if (lane == 0 && quarter == 0 && g == 0) FA_EV(20, G);

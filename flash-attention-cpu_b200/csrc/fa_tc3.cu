@@ -163,7 +163,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int s = j % NS;
         const uint32_t full = is_k ? bar_k_full(s) : bar_v_full(s);
         const uint32_t empty = is_k ? bar_k_empty(s) : bar_v_empty(s);
-        if (j >= NS) ok = mbar_wait(empty, ((j / NS) & 1) ^ 1, abort_flag, p.err);
+        if (j >= NS) ok = mbar_wait(empty, ((j / NS) & 1) ^ 1, abort_flag, p.err, p.wait_ns);
         if (!ok) break;
         mbar_expect_tx(full, 2 * C::kKBytes);
         const uint32_t base = (is_k ? sK : sV) + s * 2 * C::kKBytes;
@@ -184,13 +184,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (!skip) {
       constexpr uint32_t idesc_qk = instr_desc(kBM, BK, false);
       constexpr uint32_t idesc_pv = instr_desc(kBM, D, true);
-      bool ok = __all_sync(0xffffffffu, mbar_wait(bar_q_full, 0, abort_flag, p.err));
+      bool ok = __all_sync(0xffffffffu, mbar_wait(bar_q_full, 0, abort_flag, p.err, p.wait_ns));
       tc_fence_after();
       auto issue_pv = [&](int jj) -> bool {
         const int b = jj % NSB, s = jj % NVS;
-        if (!__all_sync(0xffffffffu, mbar_wait(bar_p_full(b), (jj / NSB) & 1, abort_flag, p.err)))
+        if (!__all_sync(0xffffffffu, mbar_wait(bar_p_full(b), (jj / NSB) & 1, abort_flag, p.err, p.wait_ns)))
           return false;
-        if (!__all_sync(0xffffffffu, mbar_wait(bar_v_full(s), (jj / NVS) & 1, abort_flag, p.err)))
+        if (!__all_sync(0xffffffffu, mbar_wait(bar_v_full(s), (jj / NVS) & 1, abort_flag, p.err, p.wait_ns)))
           return false;
         tc_fence_after();
         const uint64_t vh = smem_desc(sV + s * 2 * C::kVBytes, BK * 128, 512, kLayoutSw128Base32);
@@ -208,7 +208,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       };
       for (int j = 0; j < n_kv && ok; j++) {
         const int s = j % NKS, b = j % NSB;
-        ok = __all_sync(0xffffffffu, mbar_wait(bar_k_full(s), (j / NKS) & 1, abort_flag, p.err));
+        ok = __all_sync(0xffffffffu, mbar_wait(bar_k_full(s), (j / NKS) & 1, abort_flag, p.err, p.wait_ns));
         if (!ok) break;
         if (NSB == 1 && j > 0) {
           // single S buffer: PV(j-1) must have been issued (it reads P from it);
@@ -271,7 +271,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     float m = -INFINITY, l = 0.0f;
     for (int j = 0; j < n_kv && ok; j++) {
       const int b = j % NSB;
-      ok = __all_sync(0xffffffffu, mbar_wait(bar_s_full(b), (j / NSB) & 1, abort_flag, p.err));
+      ok = __all_sync(0xffffffffu, mbar_wait(bar_s_full(b), (j / NSB) & 1, abort_flag, p.err, p.wait_ns));
       if (!ok) break;
       tc_fence_after();
       float x[BK];
@@ -308,7 +308,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (__any_sync(0xffffffffu, need)) {
         // O is being accumulated by PV(j-1); with one S buffer PV(j-1) was
         // issued before S(j), so it has completed once S(j) is visible.
-        ok = __all_sync(0xffffffffu, mbar_wait(bar_o_done, (j - 1) & 1, abort_flag, p.err));
+        ok = __all_sync(0xffffffffu, mbar_wait(bar_o_done, (j - 1) & 1, abort_flag, p.err, p.wait_ns));
         if (!ok) break;
         tc_fence_after();
 #pragma unroll
@@ -346,10 +346,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       l += (rs[0] + rs[1]) + (rs[2] + rs[3]);
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(bar_p_full(b));
+      // (test hook: one thread of the first CTA withholds its arrive)
+      if (!(p.test_skip == j && threadIdx.x == 128 && blockIdx.x == 0 && blockIdx.z == 0))
+        mbar_arrive(bar_p_full(b));
     }
     if (n_kv > 0) {
-      const bool w = ok ? mbar_wait(bar_o_final, 0, abort_flag, p.err) : false;
+      const bool w = ok ? mbar_wait(bar_o_final, 0, abort_flag, p.err, p.wait_ns) : false;
       ok = __all_sync(0xffffffffu, w);
     }
     if (ok) {

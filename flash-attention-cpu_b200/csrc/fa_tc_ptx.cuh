@@ -43,16 +43,17 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 // Bounded wait: returns false (and raises the CTA abort flag and the global
-// error word) if the phase does not complete within kWaitLimitNs, or if another
+// error word) if the phase does not complete within limit_ns, or if another
 // role already aborted.
 __device__ __noinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity,
-                                            volatile int* abort_flag, int* err) {
+                                            volatile int* abort_flag, int* err,
+                                            unsigned long long limit_ns) {
   const unsigned long long t0 = globaltimer_ns();
   for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((it & 63u) == 0) {
       if (*abort_flag) return false;
-      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      if (globaltimer_ns() - t0 > limit_ns) {
         *abort_flag = 1;
         atomicExch(err, (int)kErrTimeout);
         return false;
@@ -62,10 +63,12 @@ __device__ __noinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity,
 }
 // The first test inline (the common case: the phase is already complete), the
 // bounded polling loop out of line.
+// Waits that ignore the abort flag (the drains of in-flight copies and MMAs
+// before exit) keep the default limit.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
-                                          int* err) {
+                                          int* err, unsigned long long limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
-  return mbar_wait_slow(bar, parity, abort_flag, err);
+  return mbar_wait_slow(bar, parity, abort_flag, err, limit_ns);
 }
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
                                             int x, int y, int z) {

@@ -132,6 +132,8 @@ def _load():
     L.fa_backward_device.restype = ctypes.c_int
     L.fa_flash_attention_backward.argtypes = [_P] * 9 + [_SZ, _SZ, _SZ, _SZ, ctypes.c_int]
     L.fa_flash_attention_backward.restype = ctypes.c_int
+    L.fa_test_stall.argtypes = [ctypes.c_int, ctypes.c_ulonglong]
+    L.fa_test_stall.restype = ctypes.c_int
     L.fa_pin_host.argtypes = [_P, _SZ]
     L.fa_pin_host.restype = ctypes.c_int
     L.fa_unpin_host.argtypes = [_P]
@@ -370,6 +372,14 @@ def pin_host(arr) -> None:
 def unpin_host(arr) -> None:
     """Undo pin_host for the same array."""
     _check(_load().fa_unpin_host(arr.ctypes.data))
+
+
+def test_stall(skip_block: int, wait_ns: int = 0) -> None:
+    """Failure-path test hook (fa_test_stall): with skip_block >= 0 the next
+    tensor-core launches withhold one softmax arrive on that key block, so
+    their bounded wait runs out after wait_ns (0: the default 2 s) and the
+    call reports FA_ERR_TIMEOUT.  test_stall(-1) restores normal operation."""
+    _check(_load().fa_test_stall(int(skip_block), int(wait_ns)))
 
 
 def last_path() -> str:

@@ -204,6 +204,17 @@ FA_API int fa_flash_attention_backward(const float* q, const float* k, const flo
  * asynchronous, so this is where their in-kernel failures surface. */
 FA_API int fa_sync_status(void* stream);
 
+/* Test hook of the failure path (no crate counterpart).  With skip_block >= 0,
+ * one softmax thread (warp) of the first CTA (pair) of every later
+ * tensor-core launch does not announce P of key block `skip_block` (counted
+ * from the CTA's first block), so the MMA issuer's bounded wait for it runs
+ * out: the kernel raises its abort flag, every role leaves, in-flight copies
+ * and MMAs are drained, tensor memory is freed, and the call reports
+ * FA_ERR_TIMEOUT.  wait_ns sets the limit of those abortable waits (0: the
+ * default of 2 s).  fa_test_stall(-1, 0) restores normal operation.  Only
+ * software arrives are withheld: no copy or MMA completion is skipped. */
+FA_API int fa_test_stall(int skip_block, unsigned long long wait_ns);
+
 /* ---- library control ---------------------------------------------------- */
 FA_API int fa_set_precision(int precision); /* fa_precision */
 FA_API int fa_get_precision(void);
