@@ -513,7 +513,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 // shared memory.  Each CTA therefore loads only half of every K tile (64 of
 // its 128 keys) and half of every V tile (64 of the 128 head columns), which
 // halves the L2->SM traffic per FLOP and doubles how many tiles the same
-// shared memory can keep in flight.  No load is multicast: each CTA's TMA
+// shared memory can keep in flight.  Every load has one destination: each CTA's TMA
 // writes only its own shared memory and signals the leader's barrier.
 //
 // Per CTA: TMEM columns Q [0, D), O [D, 2D), S/P buffers [2D, 2D + 2*BK);
