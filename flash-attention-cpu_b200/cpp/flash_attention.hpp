@@ -16,8 +16,12 @@
 // Link with -lfa_b200 (flash-attention-cpu_b200/lib).
 #pragma once
 
+#include <algorithm>
+#include <cmath>
 #include <cstddef>
+#include <limits>
 #include <span>
+#include <vector>
 #include <stdexcept>
 #include <string>
 
@@ -103,6 +107,57 @@ FA_CPP_MULTI(flash_attention_multihead_v2)
 FA_CPP_MULTI(flash_attention_multihead_v3)
 FA_CPP_MULTI(flash_attention_multihead)
 #undef FA_CPP_MULTI
+
+// ---- the crate's `naive` module (src/naive.rs:14-75) -------------------------
+// Textbook attention that materialises the [seq_len_q, seq_len_k] score
+// matrix.  In the crate it is public CPU code used as a correctness oracle and
+// a benchmark comparison point; it stays CPU code here (an API item of the
+// crate, not a fallback of the GPU forward, which never calls it).
+namespace naive {
+inline void naive_attention(std::span<const float> q, std::span<const float> k,
+                            std::span<const float> v, std::size_t seq_len_q,
+                            std::size_t seq_len_k, std::size_t d_head, bool causal,
+                            std::span<float> out) {
+  if (q.size() != seq_len_q * d_head) throw Panic("assertion failed: q.len() == seq_len_q * d_head");
+  if (k.size() != seq_len_k * d_head) throw Panic("assertion failed: k.len() == seq_len_k * d_head");
+  if (v.size() != seq_len_k * d_head) throw Panic("assertion failed: v.len() == seq_len_k * d_head");
+  if (out.size() != seq_len_q * d_head)
+    throw Panic("assertion failed: out.len() == seq_len_q * d_head");
+  const float scale = 1.0f / std::sqrt(static_cast<float>(d_head));
+  std::vector<float> p(seq_len_k);
+  for (std::size_t i = 0; i < seq_len_q; i++) {
+    const float* qi = q.data() + i * d_head;
+    // scaled scores of row i, -inf past the diagonal when causal
+    float m = -std::numeric_limits<float>::infinity();
+    for (std::size_t j = 0; j < seq_len_k; j++) {
+      if (causal && j > i) {
+        p[j] = -std::numeric_limits<float>::infinity();
+        continue;
+      }
+      const float* kj = k.data() + j * d_head;
+      float dot = 0.0f;
+      for (std::size_t c = 0; c < d_head; c++) dot += qi[c] * kj[c];
+      p[j] = dot * scale;
+      m = std::max(m, p[j]);
+    }
+    // softmax of the row (a row that sees no key keeps probability 0)
+    float sum = 0.0f;
+    for (std::size_t j = 0; j < seq_len_k; j++) {
+      p[j] = std::exp(p[j] - m);
+      sum += p[j];
+    }
+    const float inv = sum > 0.0f ? 1.0f / sum : 0.0f;
+    float* o = out.data() + i * d_head;
+    std::fill(o, o + d_head, 0.0f);
+    for (std::size_t j = 0; j < seq_len_k; j++) {
+      const float w = p[j] * inv;
+      if (w == 0.0f) continue;
+      const float* vj = v.data() + j * d_head;
+      for (std::size_t c = 0; c < d_head; c++) o[c] += w * vj[c];
+    }
+  }
+}
+}  // namespace naive
 
 // ---- beyond the crate's API (this library's additions) ---------------------
 

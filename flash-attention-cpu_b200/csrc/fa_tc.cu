@@ -523,65 +523,6 @@ __global__ void __launch_bounds__(kThreads, 1)
 // p_full are waited on only in the leader (the peer arrives on them remotely);
 // the MMA completions are committed to both CTAs' copies of k_empty, v_empty,
 // s_full, o_done, o_final and drain.
-__device__ __forceinline__ uint32_t cluster_rank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-__device__ __forceinline__ uint32_t map_to_rank(uint32_t saddr, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
-  return r;
-}
-// Arrive on a barrier of the peer CTA.  Default semantics (release at CTA
-// scope): every use follows a tcgen05.wait::st, so the TMEM data it publishes
-// is already complete; a cluster-scope release costs ~1000 cycles per arrive.
-__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_bar) {
-  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
-}
-__device__ __forceinline__ void mbar_expect_tx_cluster(uint32_t cluster_bar, uint32_t bytes) {
-  asm volatile(
-      "mbarrier.arrive.expect_tx.release.cluster.shared::cluster.b64 _, [%0], %1;" ::"r"(
-          cluster_bar),
-      "r"(bytes)
-      : "memory");
-}
-// TMA tile load into this CTA's shared memory, completing on a barrier that may
-// live in the peer CTA of the pair.
-__device__ __forceinline__ void tma_load_3d_pair(uint32_t dst, const CUtensorMap* map,
-                                                 uint32_t cluster_bar, int x, int y, int z) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.tile.mbarrier::complete_tx::"
-      "bytes [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(cluster_bar), "r"(x), "r"(y), "r"(z)
-      : "memory");
-}
-// Warp-wide forms: every lane executes them with uniform operands and one
-// elected lane issues the instruction.
-__device__ __forceinline__ void mma_ts_pair_elect(uint32_t d_tmem, uint32_t a_tmem,
-                                                  uint64_t b_desc, uint32_t idesc,
-                                                  uint32_t accum) {
-  asm volatile(
-      "{\n\t.reg .pred p, e;\n\t"
-      "elect.sync _|e, 0xffffffff;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "@e tcgen05.mma.cta_group::2.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accum)
-      : "memory");
-}
-__device__ __forceinline__ void tc_commit_pair_elect(uint32_t cluster_bar) {
-  asm volatile(
-      "{\n\t.reg .pred e;\n\t"
-      "elect.sync _|e, 0xffffffff;\n\t"
-      "@e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(
-          cluster_bar)
-      : "memory");
-}
-__device__ __forceinline__ void cluster_sync_all() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
-                   : "memory");
-}
-
 template <int D, int BK, int NKS, int NVS, int NG>
 struct PairCfg {
   static constexpr int kKHalf = BK / 2;                 // keys of a K tile held per CTA

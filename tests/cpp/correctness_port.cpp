@@ -116,6 +116,27 @@ static void cpu_cases() {
     CHECK(same, "%s sk=0 must leave out untouched", kNames[i]);
     kVariants[i](e, e, e, 4, 4, 0, {}, out);
   }
+  // the crate's `naive` module (src/naive.rs:14-75) on the CPU, against the
+  // oracle's restatement of it, over the ragged and causal shapes of the
+  // crate's tests; and its length asserts
+  const size_t shapes[][3] = {{17, 23, 32}, {1, 1, 16}, {1, 50, 33}, {50, 1, 33},
+                              {97, 131, 17}, {10, 40, 32}, {64, 64, 64}};
+  for (const auto& sh : shapes)
+    for (bool causal : {false, true}) {
+      const size_t a = sh[0], b = sh[1], dd = sh[2];
+      Vec nq = random_vec(a * dd, 7), nk = random_vec(b * dd, 8), nv = random_vec(b * dd, 9);
+      Vec got(a * dd, -1.f), want(a * dd);
+      naive::naive_attention(nq, nk, nv, a, b, dd, causal, got);
+      oracle_naive_f32(nq.data(), nk.data(), nv.data(), a, b, dd, causal, want.data());
+      CHECK(max_abs_diff(got.data(), want.data(), got.size()) < 1e-5f, "naive %zu %zu %zu %d",
+            a, b, dd, (int)causal);
+    }
+  Vec nout(sq * d);
+  CHECK(panics([&] {
+          naive::naive_attention(std::span<const float>(q).first(q.size() - 1), k, v, sq, sk, d,
+                                 false, nout);
+        }),
+        "naive q");
 }
 
 static void gpu_cases() {

@@ -32,7 +32,8 @@ def fa(gpu_lib):
     (0, (1, 100, 1000, 128, False), "single CTA, TF32"),
     (0, (2, 512, 1024, 128, True), "CTA pair, TF32, d 128"),
     (0, (2, 512, 1024, 64, False), "CTA pair, TF32, d 64"),
-    (1, (1, 100, 1000, 128, False), "3xTF32"),
+    (1, (1, 100, 1000, 128, False), "3xTF32, single CTA"),
+    (1, (2, 512, 1024, 128, True), "3xTF32, CTA pair"),
 ])
 def test_withheld_arrive_times_out_and_the_gpu_recovers(fa, prec, shape, kernel):
     bh, sq, sk, d, causal = shape
