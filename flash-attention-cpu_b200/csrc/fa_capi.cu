@@ -209,7 +209,7 @@ int dispatch(fa::FwdParams p, int dev, cudaStream_t s) {
     if (e != cudaSuccess) return cuda_err(e, "decode launch");
     return FA_OK;
   }
-  if (prec == FA_PREC_3XTF32 && (p.d == 64 || p.d == 128) && a16) {
+  if (prec == FA_PREC_3XTF32 && (p.d == 32 || p.d == 64 || p.d == 96 || p.d == 128) && a16) {
     t_path = "tcgen05_3xtf32";
     float* ws = nullptr;
     e = cudaMallocAsync((void**)&ws, fa::tc3_workspace_floats(p, st.num_sms) * sizeof(float), s);

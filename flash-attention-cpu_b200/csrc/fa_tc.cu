@@ -1237,8 +1237,12 @@ extern "C" __attribute__((visibility("default"))) int fa_trace_read(unsigned lon
 }
 #endif
 
+// d = 64, 128: the CTA-pair kernel (more than 128 query rows) and the
+// single-CTA kernel; d = 32, 96: the single-CTA kernel at every length (the
+// pair kernel splits V's columns over two CTAs in 32-column TMA boxes, so it
+// needs d % 64 == 0).
 bool tc_supported(int d, int precision) {
-  return precision == 0 && (d == 64 || d == 128);
+  return precision == 0 && (d == 32 || d == 64 || d == 96 || d == 128);
 }
 
 // Key-range splits for the pair kernel: when the work tiles (256 rows of one
@@ -1252,8 +1256,10 @@ bool tc_supported(int d, int precision) {
 // the single-CTA kernel, e.g. a chunk of a prefill against a long cache) split
 // over blockIdx.z the same way when the slices are at most half the SMs.
 int tc_pick_splits(const FwdParams& p, int num_sms) {
-  if (!(p.d == 64 || p.d == 128)) return 1;
-  if (p.sq <= kBM) {
+  if (!(p.d == 32 || p.d == 64 || p.d == 96 || p.d == 128)) return 1;
+  const bool pair = p.sq > kBM && (p.d == 64 || p.d == 128);
+  if (!pair) {
+    if (p.sq > kBM) return 1;
     // Single-CTA kernel, one CTA per slice.  Measured on one B200 (128 rows,
     // d 128): the split pays up to ~20 slices on 4096 keys (51 -> 32 us), is
     // neutral at 40 and slower at 74 (60 -> 78 us), so it needs 4 SMs per
@@ -1303,6 +1309,8 @@ cudaError_t launch_tc(const FwdParams& p, int precision, float* scratch, size_t 
   // pair kernel runs two softmax warpgroups (four measured slower: the softmax
   // phases are bound by issue and latency, not by the number of warps).
   const bool single = p.sq <= kBM;
+  if (p.d == 96) return launch_tf32<96, 128, 64, 2, 3>(p, s, split, scratch);
+  if (p.d == 32) return launch_tf32<32, 128, 128, 3, 3>(p, s, split, scratch);
   if (p.d == 128)
     return single ? launch_tf32<128, 128, 64, 2, 3>(p, s, split, scratch)
                   : launch_tf32_pair<128, 128, 2, 2, 2>(p, s, split, scratch);

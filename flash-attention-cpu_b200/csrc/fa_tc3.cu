@@ -1000,7 +1000,7 @@ static int tc3_pick_splits(const FwdParams& p, int num_sms) {
   int kend = p.sk;
   if (p.causal) kend = causal_limit(p.q_offset + p.sq - 1, p.k_offset, p.sk);
   const long long nb = (kend + 63) / 64;
-  if (p.sq > kBM) {
+  if (p.sq > kBM && (p.d == 64 || p.d == 128)) {
     const long long n_work = (long long)((p.sq + 2 * kBM - 1) / (2 * kBM)) * p.bh;
     const long long clusters = num_sms / 2;
     if (n_work * 2 > clusters) return 1;
@@ -1032,6 +1032,9 @@ cudaError_t launch_tc3(const FwdParams& p, float* ws, int num_sms, cudaStream_t 
   }
   if (p.d == 128) return launch_3x<128, 64, 2, 1, 1>(p, ws, split, s);
   if (p.d == 64) return launch_3x<64, 64, 3, 3, 2>(p, ws, split, s);
+  // d = 32, 96: the single-CTA kernel at every length (see tc_supported)
+  if (p.d == 96) return launch_3x<96, 64, 2, 1, 1>(p, ws, split, s);
+  if (p.d == 32) return launch_3x<32, 64, 3, 3, 2>(p, ws, split, s);
   return cudaErrorInvalidValue;
 }
 

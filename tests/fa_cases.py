@@ -36,12 +36,16 @@ AGREEMENT_CASES = [
     (200, 200, 128, 64, 128, True),
 ]
 
-# Shapes the tensor-core kernel tiles (d = 64, 128), ragged and causal, incl. Sq != Sk.
+# Shapes the tensor-core kernels tile (d = 32, 64, 96, 128), ragged and causal, incl. Sq != Sk.
 TC_CASES = [
     (128, 128, 64, True), (128, 128, 128, True), (200, 200, 128, True), (200, 200, 128, False),
     (300, 77, 64, False), (77, 300, 64, True), (77, 300, 128, True), (513, 1000, 128, True),
     (1000, 513, 64, True), (256, 4096, 128, False), (4096, 256, 64, True), (130, 130, 64, False),
     (33, 700, 128, True), (700, 33, 128, False), (129, 129, 128, True),
+    # d = 32 and 96 (the crate's tests use 32; 96 is a common head size): the
+    # single-CTA tcgen05 kernels at every length
+    (128, 128, 32, True), (513, 1000, 32, True), (77, 300, 32, False), (300, 77, 96, False),
+    (200, 200, 96, True), (1000, 513, 96, True), (2048, 2048, 96, False), (100, 5000, 96, True),
 ]
 
 
