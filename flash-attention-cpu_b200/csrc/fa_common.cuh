@@ -107,6 +107,12 @@ size_t tc_scratch_floats(const FwdParams& p, int num_sms);
 // (hi/lo planes of K and V, then the key-range partials of small launches).
 size_t tc3_workspace_floats(const FwdParams& p, int num_sms);
 cudaError_t launch_tc3(const FwdParams& p, float* ws, int num_sms, cudaStream_t s);
+// Schedule model of the persistent CTA-pair kernels (fa_tc.cu): the longest
+// per-cluster work in key blocks of `bk` keys, and the cost of merging
+// n_split partials per row (microseconds).
+double pair_schedule_makespan(const FwdParams& p, int n_split, int clusters, int bk,
+                              double tile_cost);
+double merge_cost_us(const FwdParams& p, int n_split);
 unsigned long long launches_issued();
 void count_launch(int n = 1);
 

@@ -50,6 +50,9 @@
 //   Q / O (pair kernel) [D/32 chunks][128 rows][32], 128B swizzle.
 #include "fa_tc_ptx.cuh"
 
+#include <algorithm>
+#include <vector>
+
 namespace fa {
 namespace {
 
@@ -1255,6 +1258,40 @@ bool tc_supported(int d, int precision) {
 // and are left whole.  Launches of at most 128 query rows (one CTA per slice in
 // the single-CTA kernel, e.g. a chunk of a prefill against a long cache) split
 // over blockIdx.z the same way when the slices are at most half the SMs.
+// Longest per-cluster sum of work-unit costs under the pair kernels' static
+// schedule (units in dispatch order, dealt to the clusters in snake rounds),
+// in key blocks of `bk` keys; each unit also costs `tile_cost` blocks (its
+// tile change).  Mirrors tile_of / work_of of the kernels.
+double pair_schedule_makespan(const FwdParams& p, int n_split, int clusters, int bk,
+                              double tile_cost) {
+  const int n_pairs = (p.sq + 2 * kBM - 1) / (2 * kBM);
+  const long long n_work = (long long)n_pairs * p.bh * n_split;
+  if (n_work <= 0 || clusters <= 0) return 0.0;
+  std::vector<double> load(clusters, 0.0);
+  for (long long u = 0; u < n_work; u++) {
+    const long long w = u / n_split;
+    const int sp = (int)(u % n_split);
+    const int pair = p.causal ? n_pairs - 1 - (int)(w / p.bh) : (int)(w % n_pairs);
+    const int q0 = pair * 2 * kBM;
+    const int rows = std::min(2 * kBM, p.sq - q0);
+    int kend = p.sk;
+    if (p.causal) kend = causal_limit(p.q_offset + q0 + rows - 1, p.k_offset, p.sk);
+    const long long nb = (kend + bk - 1) / bk;
+    const long long n_kv = (sp + 1) * nb / n_split - sp * nb / n_split;
+    const long long k = u / clusters, i = u % clusters;
+    load[(k & 1) ? clusters - 1 - i : i] += (double)n_kv + tile_cost;
+  }
+  return *std::max_element(load.begin(), load.end());
+}
+
+// Cost in microseconds of merging n_split partials per row: the extra partial
+// outputs the kernel writes, and the LSE combine launch that reads them all.
+double merge_cost_us(const FwdParams& p, int n_split) {
+  const double rows = (double)p.bh * p.sq;
+  const double bytes = rows * (p.d + 1) * 4.0 * (2.0 * n_split);
+  return 4.0 + bytes / 5.0e6;  // ~5 TB/s, plus launch and tail
+}
+
 int tc_pick_splits(const FwdParams& p, int num_sms) {
   if (!(p.d == 32 || p.d == 64 || p.d == 96 || p.d == 128)) return 1;
   const bool pair = p.sq > kBM && (p.d == 64 || p.d == 128);
@@ -1279,7 +1316,26 @@ int tc_pick_splits(const FwdParams& p, int num_sms) {
   const long long n_pairs = (p.sq + 2 * kBM - 1) / (2 * kBM);
   const long long n_work = n_pairs * p.bh;
   const long long clusters = num_sms / 2;
-  if (n_work * 2 > clusters) return 1;
+  if (n_work > 2 * clusters) return 1;
+  if (n_work * 2 > clusters) {
+    // One or two rounds of tiles: the longest cluster sets the time.  Causal
+    // tiles differ up to the whole key range, so a few heavy tiles can leave
+    // most clusters idle (32 x 4096 x 128 over 8 GPUs: 64 tiles of 2..32 key
+    // blocks on 74 clusters).  Split every tile's keys in two or three when
+    // the schedule model says the shorter longest cluster pays for the merge.
+    const double t_blk = p.d == 128 ? 1.35 : 0.75;  // us per 128-key block, one B200
+    double best = 0.0;
+    int best_s = 1;
+    for (int sp = 1; sp <= 3; sp++) {
+      const double t = pair_schedule_makespan(p, sp, (int)clusters, 128, 1.2) * t_blk +
+                       (sp > 1 ? merge_cost_us(p, sp) : 0.0);
+      if (sp == 1 || t < best) {
+        best = t;
+        best_s = sp;
+      }
+    }
+    return best_s;
+  }
   int kend = p.sk;
   if (p.causal) kend = causal_limit(p.q_offset + p.sq - 1, p.k_offset, p.sk);
   const long long max_nkv = (kend + 127) / 128;

@@ -1003,7 +1003,24 @@ static int tc3_pick_splits(const FwdParams& p, int num_sms) {
   if (p.sq > kBM && (p.d == 64 || p.d == 128)) {
     const long long n_work = (long long)((p.sq + 2 * kBM - 1) / (2 * kBM)) * p.bh;
     const long long clusters = num_sms / 2;
-    if (n_work * 2 > clusters) return 1;
+    if (n_work > 2 * clusters) return 1;
+    if (n_work * 2 > clusters) {
+      // one or two rounds of tiles: split the keys when the schedule model
+      // (pair_schedule_makespan, shared with the TF32 pair kernel) says the
+      // shorter longest cluster pays for the merge
+      const double t_blk = p.d == 128 ? 1.8 : 1.0;  // us per 64-key block, one B200
+      double best = 0.0;
+      int best_s = 1;
+      for (int sp = 1; sp <= 3; sp++) {
+        const double t = pair_schedule_makespan(p, sp, (int)clusters, 64, 2.0) * t_blk +
+                         (sp > 1 ? merge_cost_us(p, sp) : 0.0);
+        if (sp == 1 || t < best) {
+          best = t;
+          best_s = sp;
+        }
+      }
+      return best_s;
+    }
     long long split = clusters / n_work;
     if (split > nb / 8) split = nb / 8;
     if (split > 16) split = 16;
