@@ -264,32 +264,69 @@ __global__ void __launch_bounds__(256) decode_fwd(FwdParams p, int chunk, float*
   if (threadIdx.x == 0 && dst_lse) *dst_lse = lse_v;
 }
 
-// Log-sum-exp merge of n partials per row.  One 128-thread CTA per row.
-__global__ void __launch_bounds__(128) lse_combine(const float* __restrict__ o_parts,
+// Log-sum-exp merge of n partials per row: one warp per row, 8 rows per CTA.
+// The lanes reduce the row's max and sum over the parts, then each lane owns
+// 4 (or 1) output columns and accumulates the parts with weights broadcast by
+// shuffle, 32 parts at a time.
+template <bool V4>
+__global__ void __launch_bounds__(256) lse_combine(const float* __restrict__ o_parts,
                                                    const float* __restrict__ lse_parts,
                                                    int n, long long rows, int d,
                                                    float* __restrict__ out,
                                                    float* __restrict__ lse_out) {
-  const long long row = blockIdx.x;
+  const int lane = threadIdx.x & 31;
+  const long long row = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (row >= rows) return;  // (whole warps leave together)
   float M = -INFINITY;
-  for (int p = 0; p < n; p++) M = fmaxf(M, lse_parts[(size_t)p * rows + row]);
+  for (int p = lane; p < n; p += 32) M = fmaxf(M, lse_parts[(size_t)p * rows + row]);
+  M = warp_max(M);
   float L = 0.0f;
   if (M != -INFINITY)
-    for (int p = 0; p < n; p++) {
-      float lp = lse_parts[(size_t)p * rows + row];
+    for (int p = lane; p < n; p += 32) {
+      const float lp = lse_parts[(size_t)p * rows + row];
       if (lp != -INFINITY) L += expf(lp - M);
     }
+  L = warp_sum(L);
   const float inv_L = L > 0.0f ? 1.0f / L : 0.0f;
-  for (int c = threadIdx.x; c < d; c += blockDim.x) {
-    float o = 0.0f;
-    if (M != -INFINITY)
-      for (int p = 0; p < n; p++) {
-        float lp = lse_parts[(size_t)p * rows + row];
-        if (lp != -INFINITY) o = fmaf(expf(lp - M), o_parts[((size_t)p * rows + row) * d + c], o);
+  constexpr int W = V4 ? 4 : 1;
+  for (int c0 = 0; c0 < d; c0 += 32 * W) {
+    const int c = c0 + lane * W;
+    const bool active = c < d;
+    float acc[W];
+#pragma unroll
+    for (int e = 0; e < W; e++) acc[e] = 0.0f;
+    for (int p0 = 0; p0 < n && M != -INFINITY; p0 += 32) {
+      float w = 0.0f;
+      if (p0 + lane < n) {
+        const float lp = lse_parts[(size_t)(p0 + lane) * rows + row];
+        if (lp != -INFINITY) w = expf(lp - M);
       }
-    out[row * d + c] = o * inv_L;
+      const int cnt = min(32, n - p0);
+      for (int i = 0; i < cnt; i++) {
+        const float wi = __shfl_sync(0xffffffffu, w, i);
+        if (wi == 0.0f || !active) continue;
+        const float* src = o_parts + ((size_t)(p0 + i) * rows + row) * d + c;
+        if constexpr (V4) {
+          const float4 o = *reinterpret_cast<const float4*>(src);
+          acc[0] = fmaf(wi, o.x, acc[0]);
+          acc[1] = fmaf(wi, o.y, acc[1]);
+          acc[2] = fmaf(wi, o.z, acc[2]);
+          acc[3] = fmaf(wi, o.w, acc[3]);
+        } else {
+          acc[0] = fmaf(wi, *src, acc[0]);
+        }
+      }
+    }
+    if (active) {
+      float* dst = out + (size_t)row * d + c;
+      if constexpr (V4)
+        *reinterpret_cast<float4*>(dst) =
+            make_float4(acc[0] * inv_L, acc[1] * inv_L, acc[2] * inv_L, acc[3] * inv_L);
+      else
+        *dst = acc[0] * inv_L;
+    }
   }
-  if (threadIdx.x == 0 && lse_out) lse_out[row] = (L > 0.0f) ? M + logf(L) : -INFINITY;
+  if (lane == 0 && lse_out) lse_out[row] = (L > 0.0f) ? M + logf(L) : -INFINITY;
 }
 
 template <int DCH>
@@ -395,8 +432,12 @@ cudaError_t launch_combine(const float* o_parts, const float* lse_parts, int n_p
                            long long rows, int d, float* out, float* lse_out,
                            cudaStream_t s) {
   if (rows <= 0) return cudaSuccess;
-  lse_combine<<<(unsigned)rows, 128, 0, s>>>(o_parts, lse_parts, n_parts, rows, d, out,
-                                             lse_out);
+  const unsigned grid = (unsigned)((rows + 7) / 8);
+  const bool v4 = (d % 4) == 0 && (((uintptr_t)o_parts | (uintptr_t)out) & 15) == 0;
+  if (v4)
+    lse_combine<true><<<grid, 256, 0, s>>>(o_parts, lse_parts, n_parts, rows, d, out, lse_out);
+  else
+    lse_combine<false><<<grid, 256, 0, s>>>(o_parts, lse_parts, n_parts, rows, d, out, lse_out);
   count_launch();
   return cudaGetLastError();
 }

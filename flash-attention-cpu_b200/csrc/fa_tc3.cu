@@ -334,7 +334,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t rh[32], rl[32];
 #pragma unroll
         for (int e = 0; e < 32; e++) {
-          const float pe = exp2f(__fadd_rn(__fmul_rn(x[c * 32 + e], c_log2), neg_m));
+          const float pe = ex2(__fadd_rn(__fmul_rn(x[c * 32 + e], c_log2), neg_m));
           const float h = hi_part(pe);
           rs[e & 3] += pe;
           rh[e] = __float_as_uint(h);
@@ -857,7 +857,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           uint32_t rh[32], rl[32];
 #pragma unroll
           for (int e = 0; e < 32; e++) {
-            const float pe = exp2f(__fadd_rn(__fmul_rn(x[c * 32 + e], c_log2), neg_m));
+            const float pe = ex2(__fadd_rn(__fmul_rn(x[c * 32 + e], c_log2), neg_m));
             const float h = hi_part(pe);
             rs[e & 3] += pe;
             rh[e] = __float_as_uint(h);
