@@ -537,7 +537,7 @@ struct PairCfg {
   static constexpr int kOffV = NKS * kKBytes;
   static constexpr int kOffQ = kOffV + NVS * kVBytes;   // D/32 swizzled [128 x 32] chunks
   static constexpr int kOffBar = kOffQ + kQBytes;
-  static constexpr int kNumBars = 1 + 2 * NKS + 2 * NVS + 2 + 2 + 3 + 2;
+  static constexpr int kNumBars = 1 + 2 * NKS + 2 * NVS + 2 + 2 + 3 + 2 + 1;
   static constexpr int kOffRed = (kOffBar + kNumBars * 8 + 16 + 15) / 16 * 16;
   // softmax exchange: row maxima [2 blocks][NG][128], row sums [2 tiles][NG][128]
   static constexpr int kSmemBytes = kOffRed + 4 * NG * 128 * 4 + 1024;
@@ -586,10 +586,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(NG), 1)
   constexpr uint32_t kB2 = 1 + 2 * NKS + 2 * NVS;
   auto bar_s_full = [&](int b) { return bar0 + 8u * (kB2 + b); };
   auto bar_p_full = [&](int b) { return bar0 + 8u * (kB2 + 2 + b); };
-  // o_done completes once per PV (global order).  A wait on it for PV(G-1) at
-  // softmax block G is unambiguous: S(G) was issued after PV(G-2), so when S(G)
-  // is visible at most PV(G-1) and PV(G) remain, and PV(G) needs P(G).
-  const uint32_t bar_o_done = bar0 + 8u * (kB2 + 4);
+  // o_done(b) completes once per PV of the blocks G with G % 2 == b.
+  auto bar_o_done = [&](int b) { return bar0 + 8u * (b == 0 ? kB2 + 4 : kB2 + 9); };
+  // A K slot is free once the QK^T that read it has completed, and a V slot
+  // once its PV has: with two slots, slot G % 2 frees exactly when S buffer
+  // G % 2 fills (s_full) or PV(G) completes (o_done(G % 2)), so the producers
+  // wait on those and the MMA warp commits no separate "empty" barriers.
+  constexpr bool kKShare = NKS == 2, kVShare = NVS == 2;
   const uint32_t bar_drain = bar0 + 8u * (kB2 + 5);
   // o_final completes once per work tile (its last PV, or at once for a tile
   // that sees no key).  The next tile's first PV needs P of its first block,
@@ -684,7 +687,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(NG), 1)
       mbar_init(bar_s_full(b), 1);
       mbar_init(bar_p_full(b), 8 * NG);
     }
-    mbar_init(bar_o_done, 1);
+    mbar_init(bar_o_done(0), 1);
+    mbar_init(bar_o_done(1), 1);
     mbar_init(bar_drain, 1);
     mbar_init(bar_o_final, 1);
     mbar_init(bar_q_smem_full, 1);  // warp 3
@@ -721,9 +725,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(NG), 1)
         const Tile t = tile_of(w);
         for (int j = 0; j < t.n_kv && ok; j++, G++) {
           const int s = G % NS;
-          if (G >= NS)
-            ok = mbar_wait(is_k ? bar_k_empty(s) : bar_v_empty(s), ((G / NS) & 1) ^ 1, abort_flag,
-                           p.err, p.wait_ns);
+          if (G >= NS) {
+            const uint32_t empty = is_k ? (kKShare ? bar_s_full(G & 1) : bar_k_empty(s))
+                                        : (kVShare ? bar_o_done(G & 1) : bar_v_empty(s));
+            ok = mbar_wait(empty, ((G / NS) & 1) ^ 1, abort_flag, p.err, p.wait_ns);
+          }
           if (!ok) break;
           FA_EV(is_k ? 12 : 11, G);
           const uint32_t full = at_leader(is_k ? bar_k_full(s) : bar_v_full(s));
@@ -776,8 +782,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(NG), 1)
         for (int kk = 0; kk < BK / 8; kk++)
           mma_ts_pair_elect(t_o, t_s(b) + kk * 8, vdesc + (uint64_t)(kk * 64), idesc_pv,
                             (j > 0 || kk > 0) ? 1u : 0u);
-        commit_both(bar_v_empty(sv));
-        commit_both(bar_o_done);
+        if (!kVShare) commit_both(bar_v_empty(sv));
+        commit_both(bar_o_done(G & 1));
         if (lane == 0) FA_EV(4, G);
         return true;
       };
@@ -804,7 +810,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(NG), 1)
                               kdesc + (uint64_t)(((kk >> 2) * C::kKHalf * 128 + (kk & 3) * 32) >> 4),
                               idesc_qk, kk > 0 ? 1u : 0u);
           commit_both(bar_s_full(b));
-          commit_both(bar_k_empty(s));
+          if (!kKShare) commit_both(bar_k_empty(s));
           if (lane == 0) FA_EV(1, Gj);
           if (j > 0) ok = issue_pv(Gj - 1, j - 1);
         }
@@ -1065,7 +1071,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(NG), 1)
           m = m_new;
         }
         if (__any_sync(0xffffffffu, need) &&
-            __all_sync(0xffffffffu, mbar_wait(bar_o_done, (Gj - 1) & 1, abort_flag, p.err, p.wait_ns))) {
+            __all_sync(0xffffffffu, mbar_wait(bar_o_done((Gj - 1) & 1), ((Gj - 1) >> 1) & 1, abort_flag,
+                                            p.err, p.wait_ns))) {
           // (a failed wait raises the abort flag; the loop then ends at the
           // next block's bar_any)
           tc_fence_after();

@@ -425,7 +425,7 @@ struct Tc3PairCfg {
   static constexpr int kOffK = kOffQ + kQBytes;           // NKS x (hi, lo)
   static constexpr int kOffV = kOffK + NKS * 2 * kKPlane;  // NVS x (hi, lo)
   static constexpr int kOffBar = kOffV + NVS * 2 * kVPlane;
-  static constexpr int kNumBars = 1 + 2 * NKS + 2 * NVS + 2 * NSB + 5;
+  static constexpr int kNumBars = 1 + 2 * NKS + 2 * NVS + 2 * NSB + 5 + (NSB - 1);
   static constexpr int kSmemBytes = kOffBar + kNumBars * 8 + 16 + 1024;
   static constexpr int kTmemColsUsed = 2 * D + NSB * 2 * BK;
   static constexpr int kTmemCols = kTmemColsUsed <= 256 ? 256 : 512;
@@ -463,9 +463,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   constexpr uint32_t kB2 = 1 + 2 * NKS + 2 * NVS;
   auto bar_s_full = [&](int b) { return bar0 + 8u * (kB2 + b); };
   auto bar_p_full = [&](int b) { return bar0 + 8u * (kB2 + NSB + b); };
-  // o_done completes once per PV; a wait for PV(G-1) at softmax block G is
-  // unambiguous because S(G) was issued after PV(G-2) (see the TF32 pair kernel).
-  const uint32_t bar_o_done = bar0 + 8u * (kB2 + 2 * NSB);
+  // o_done(b) completes once per PV of the blocks G with G % NSB == b.  A K
+  // slot is free once the QK^T that read it has completed, and a V slot once
+  // its PV has: with as many slots as S buffers, slot G % NSB frees exactly
+  // when S buffer G % NSB fills (s_full) or PV(G) completes (o_done), so the
+  // producers wait on those and no separate "empty" barriers are committed.
+  auto bar_o_done = [&](int b) {
+    return bar0 + 8u * (b == 0 ? kB2 + 2 * NSB : kB2 + 2 * NSB + 4 + b);
+  };
+  constexpr bool kKShare = NKS == NSB, kVShare = NVS == NSB;
   const uint32_t bar_drain = bar0 + 8u * (kB2 + 2 * NSB + 1);
   const uint32_t bar_o_final = bar0 + 8u * (kB2 + 2 * NSB + 2);  // once per tile
   const uint32_t bar_q_smem_full = bar0 + 8u * (kB2 + 2 * NSB + 3);   // Q landed (local TMA)
@@ -532,7 +538,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       mbar_init(bar_s_full(b), 1);
       mbar_init(bar_p_full(b), 8);
     }
-    mbar_init(bar_o_done, 1);
+    for (int b = 0; b < NSB; b++) mbar_init(bar_o_done(b), 1);
     mbar_init(bar_drain, 1);
     mbar_init(bar_o_final, 1);
     mbar_init(bar_q_smem_full, 1);
@@ -570,9 +576,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         const Tile t = tile_of(w);
         for (int j = 0; j < t.n_kv && ok; j++, G++) {
           const int s = G % NS;
-          if (G >= NS)
-            ok = mbar_wait(is_k ? bar_k_empty(s) : bar_v_empty(s), ((G / NS) & 1) ^ 1, abort_flag,
-                           p.err, p.wait_ns);
+          if (G >= NS) {
+            const uint32_t empty = is_k ? (kKShare ? bar_s_full(G % NSB) : bar_k_empty(s))
+                                        : (kVShare ? bar_o_done(G % NSB) : bar_v_empty(s));
+            ok = mbar_wait(empty, ((G / NS) & 1) ^ 1, abort_flag, p.err, p.wait_ns);
+          }
           if (!ok) break;
           const uint32_t full = at_leader(is_k ? bar_k_full(s) : bar_v_full(s));
           if (is_k) {
@@ -634,8 +642,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           mma_ts_pair_elect(t_o, t_s(b) + kk * 8, vl + o, idesc_pv, 1u);
           mma_ts_pair_elect(t_o, t_pl(b) + kk * 8, vh + o, idesc_pv, 1u);
         }
-        commit_both(bar_v_empty(sv));
-        commit_both(bar_o_done);
+        if (!kVShare) commit_both(bar_v_empty(sv));
+        commit_both(bar_o_done(G % NSB));
         return true;
       };
       bool ok = true;
@@ -664,7 +672,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             mma_ts_pair_elect(t_s(b), t_ql + kk * 8, kh + ko, idesc_qk, 1u);
           }
           commit_both(bar_s_full(b));
-          commit_both(bar_k_empty(s));
+          if (!kKShare) commit_both(bar_k_empty(s));
           if (j == t.n_kv - 1) commit_both(bar_q_smem_empty);  // the tile's last QK^T
           if (j > 0) ok = issue_pv(Gj - 1, j - 1);
         }
@@ -834,8 +842,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
         if (__any_sync(0xffffffffu, need)) {
           // O is being accumulated by PV(G-1): wait for it, then rescale in TMEM
-          ok = __all_sync(0xffffffffu, mbar_wait(bar_o_done, (Gj - 1) & 1, abort_flag, p.err,
-                                                 p.wait_ns));
+          ok = __all_sync(0xffffffffu, mbar_wait(bar_o_done((Gj - 1) % NSB), ((Gj - 1) / NSB) & 1,
+                                                 abort_flag, p.err, p.wait_ns));
           if (!ok) break;
           tc_fence_after();
 #pragma unroll
