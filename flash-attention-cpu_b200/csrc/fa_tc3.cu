@@ -425,7 +425,7 @@ struct Tc3PairCfg {
   static constexpr int kOffK = kOffQ + kQBytes;           // NKS x (hi, lo)
   static constexpr int kOffV = kOffK + NKS * 2 * kKPlane;  // NVS x (hi, lo)
   static constexpr int kOffBar = kOffV + NVS * 2 * kVPlane;
-  static constexpr int kNumBars = 1 + 2 * NKS + 2 * NVS + 2 * NSB + 5 + (NSB - 1) + NKS + NVS;
+  static constexpr int kNumBars = 1 + 2 * NKS + 2 * NVS + 2 * NSB + 5 + (NSB - 1);
   static constexpr int kSmemBytes = kOffBar + kNumBars * 8 + 16 + 1024;
   static constexpr int kTmemColsUsed = 2 * D + NSB * 2 * BK;
   static constexpr int kTmemCols = kTmemColsUsed <= 256 ? 256 : 512;
@@ -438,7 +438,9 @@ struct Tc3PairCfg {
 template <int D, int BK, int NKS, int NVS, int NSB>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     tc_fwd_3xtf32_pair(const __grid_constant__ CUtensorMap tmKh,
+                       const __grid_constant__ CUtensorMap tmKl,
                        const __grid_constant__ CUtensorMap tmVh,
+                       const __grid_constant__ CUtensorMap tmVl,
                        const __grid_constant__ CUtensorMap tmQ, FwdParams p, int n_pairs,
                        int n_split, float* split_o, float* split_lse) {
   using C = Tc3PairCfg<D, BK, NKS, NVS, NSB>;
@@ -470,12 +472,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     return bar0 + 8u * (b == 0 ? kB2 + 2 * NSB : kB2 + 2 * NSB + 4 + b);
   };
   constexpr bool kKShare = NKS == NSB, kVShare = NVS == NSB;
-  // raw_k / raw_v (this CTA's): the raw (hi) plane of a K or V block has
-  // landed (local TMA).  Warp 3 then writes its lo plane and arrives on the
-  // leader's k_full / v_full, which count one arrival per CTA.
-  constexpr uint32_t kBRaw = kB2 + 2 * NSB + 5 + (NSB - 1);
-  auto bar_raw_k = [&](int s) { return bar0 + 8u * (kBRaw + s); };
-  auto bar_raw_v = [&](int s) { return bar0 + 8u * (kBRaw + NKS + s); };
   const uint32_t bar_drain = bar0 + 8u * (kB2 + 2 * NSB + 1);
   const uint32_t bar_o_final = bar0 + 8u * (kB2 + 2 * NSB + 2);  // once per tile
   const uint32_t bar_q_smem_full = bar0 + 8u * (kB2 + 2 * NSB + 3);   // Q landed (local TMA)
@@ -543,8 +539,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       mbar_init(bar_p_full(b), 8);
     }
     for (int b = 0; b < NSB; b++) mbar_init(bar_o_done(b), 1);
-    for (int s = 0; s < NKS; s++) mbar_init(bar_raw_k(s), 1);
-    for (int s = 0; s < NVS; s++) mbar_init(bar_raw_v(s), 1);
     mbar_init(bar_drain, 1);
     mbar_init(bar_o_final, 1);
     mbar_init(bar_q_smem_full, 1);
@@ -570,8 +564,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const bool skip = *abort_flag != 0;
 
   if (warp == 0 || warp == 2) {
-    // ------------------------------ TMA producers (one lane): warp 0 the raw K
-    // halves, warp 2 the raw V halves, each onto this CTA's raw barrier
+    // ------------------------------ TMA producers: warp 0 K halves, warp 2 V halves
     const bool is_k = warp == 0;
     const int NS = is_k ? NKS : NVS;
     if (lane == 0 && !skip) {
@@ -589,26 +582,34 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             ok = mbar_wait(empty, ((G / NS) & 1) ^ 1, abort_flag, p.err, p.wait_ns);
           }
           if (!ok) break;
+          const uint32_t full = at_leader(is_k ? bar_k_full(s) : bar_v_full(s));
           if (is_k) {
-            mbar_expect_tx(bar_raw_k(s), C::kKPlane);
+            mbar_expect_tx_cluster(full, 2 * C::kKPlane);
             const uint32_t base = sK + s * 2 * C::kKPlane;
             const int y = (t.j0 + j) * BK + (int)rank * C::kKHalf;
-            for (int c = 0; c < D / 32; c++)
-              tma_load_3d(base + c * C::kKHalf * 128, &tmKh, bar_raw_k(s), 32 * c, y, t.bh);
+            for (int c = 0; c < D / 32; c++) {
+              tma_load_3d_pair(base + c * C::kKHalf * 128, &tmKh, full, 32 * c, y, t.bh);
+              tma_load_3d_pair(base + C::kKPlane + c * C::kKHalf * 128, &tmKl, full, 32 * c, y,
+                               t.bh);
+            }
           } else {
-            mbar_expect_tx(bar_raw_v(s), C::kVPlane);
+            mbar_expect_tx_cluster(full, 2 * C::kVPlane);
             const uint32_t base = sV + s * 2 * C::kVPlane;
             const int y = (t.j0 + j) * BK;
-            for (int c = 0; c < C::kDHalf / 32; c++)
-              tma_load_3d(base + c * BK * 128, &tmVh, bar_raw_v(s), (int)rank * C::kDHalf + 32 * c,
-                          y, t.bh);
+            for (int c = 0; c < C::kDHalf / 32; c++) {
+              const int x = (int)rank * C::kDHalf + 32 * c;
+              tma_load_3d_pair(base + c * BK * 128, &tmVh, full, x, y, t.bh);
+              tma_load_3d_pair(base + C::kVPlane + c * BK * 128, &tmVl, full, x, y, t.bh);
+            }
           }
         }
       }
-      // no TMA write may land after the CTA exits, even when a consumer aborted
+      // no TMA write may land after the CTAs exit, even when a consumer aborted
       volatile int no_abort = 0;
-      for (int g = max(0, G - NS); g < G; g++)
-        mbar_wait(is_k ? bar_raw_k(g % NS) : bar_raw_v(g % NS), (g / NS) & 1, &no_abort, p.err);
+      if (leader)
+        for (int g = max(0, G - NS); g < G; g++)
+          mbar_wait(is_k ? bar_k_full(g % NS) : bar_v_full(g % NS), (g / NS) & 1, &no_abort,
+                    p.err);
     }
     __syncwarp();
   } else if (warp == 1) {
@@ -627,8 +628,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         if (!__all_sync(0xffffffffu, mbar_wait(bar_p_full(b), (G / NSB) & 1, abort_flag, p.err,
                                                p.wait_ns)))
           return false;
-        if (!__all_sync(0xffffffffu, mbar_wait_cl(bar_v_full(sv), (G / NVS) & 1, abort_flag, p.err,
-                                                  p.wait_ns)))
+        if (!__all_sync(0xffffffffu, mbar_wait(bar_v_full(sv), (G / NVS) & 1, abort_flag, p.err,
+                                               p.wait_ns)))
           return false;
         tc_fence_after();
         const uint64_t vh =
@@ -656,8 +657,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         tc_fence_after();
         for (int j = 0; j < t.n_kv && ok; j++) {
           const int Gj = G + j, s = Gj % NKS, b = Gj % NSB;
-          ok = __all_sync(0xffffffffu, mbar_wait_cl(bar_k_full(s), (Gj / NKS) & 1, abort_flag,
-                                                    p.err, p.wait_ns));
+          ok = __all_sync(0xffffffffu, mbar_wait(bar_k_full(s), (Gj / NKS) & 1, abort_flag, p.err,
+                                                 p.wait_ns));
           if (!ok) break;
           tc_fence_after();
           const uint64_t kh = smem_desc(sK + s * 2 * C::kKPlane, 16, 1024, kLayoutSw128);
@@ -687,21 +688,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     }
     __syncwarp();
   } else if (warp == 3) {
-    // ------------------------------ lo planes and Q loads (whole warp).  For
-    // every key block, once its raw K (V) half has landed: lo = x - hi(x) into
-    // the lo plane, element by element at the same offsets (so the swizzle
-    // does not matter), then release it to the leader's MMA warp.  K runs one
-    // block ahead of V (the MMA order is S(G+1) before PV(G)).  Between tiles:
-    // the next tile's Q, once the previous tile's QK^T has read the buffer.
-    if (!skip) {
+    // ------------------------------ Q loader (one lane): this CTA's 128 rows of
+    // each tile into the Q buffer, once the previous tile's QK^T has read it
+    if (lane == 0 && !skip) {
       bool ok = true;
-      int it = 0, qit = 0, G = 0, Gk = 0;
+      int it = 0, qit = 0;
       auto load_q = [&](const Tile& q) {
-        if (lane == 0) {
-          mbar_expect_tx(bar_q_smem_full, C::kQBytes);
-          for (int c = 0; c < D / 32; c++)
-            tma_load_3d(sQ + c * (kBM * 128), &tmQ, bar_q_smem_full, 32 * c, q.q0, q.bh);
-        }
+        mbar_expect_tx(bar_q_smem_full, C::kQBytes);
+        for (int c = 0; c < D / 32; c++)
+          tma_load_3d(sQ + c * (kBM * 128), &tmQ, bar_q_smem_full, 32 * c, q.q0, q.bh);
         qit++;
       };
       auto next_work = [&](int k) {
@@ -709,50 +704,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           if (work_of(k2) < n_work) return k2;
         return -1;
       };
-      auto convert = [&](bool is_k, int g) -> bool {
-        const int NS = is_k ? NKS : NVS, s = g % NS;
-        const int plane = is_k ? C::kKPlane : C::kVPlane;
-        if (!__all_sync(0xffffffffu, mbar_wait(is_k ? bar_raw_k(s) : bar_raw_v(s), (g / NS) & 1,
-                                               abort_flag, p.err, p.wait_ns)))
-          return false;
-        uint8_t* base = smem + (is_k ? C::kOffK : C::kOffV) + (size_t)s * 2 * plane;
-        const float4* hi = reinterpret_cast<const float4*>(base);
-        float4* lo = reinterpret_cast<float4*>(base + plane);
-#pragma unroll 4
-        for (int i = lane; i < plane / 16; i += 32) {
-          const float4 x = hi[i];
-          lo[i] = make_float4(x.x - hi_part(x.x), x.y - hi_part(x.y), x.z - hi_part(x.z),
-                              x.w - hi_part(x.w));
-        }
-        fence_proxy_async_smem();  // the lo plane is read by the tensor core
-        __syncwarp();
-        if (lane == 0)
-          mbar_arrive_cluster_release(at_leader(is_k ? bar_k_full(s) : bar_v_full(s)));
-        return true;
-      };
-      int g_total = 0;  // key blocks of this cluster's whole schedule
-      for (int k = next_work(-1); k >= 0; k = next_work(k)) g_total += tile_of(work_of(k)).n_kv;
       const int k0 = next_work(-1);
       if (k0 >= 0) load_q(tile_of(work_of(k0)));
       for (int k = k0; k >= 0 && ok; k = next_work(k)) {
-        const Tile t = tile_of(work_of(k));
-        for (int j = 0; j < t.n_kv && ok; j++) {
-          const int Gj = G + j;
-          while (ok && Gk < Gj + 2 && Gk < g_total) ok = convert(true, Gk++);
-          if (ok) ok = convert(false, Gj);
-        }
-        G += t.n_kv;
-        if (!ok) break;
         const int kn = next_work(k);
         if (kn < 0) break;
-        ok = __all_sync(0xffffffffu, mbar_wait(bar_q_smem_empty, it & 1, abort_flag, p.err,
-                                               p.wait_ns));
+        ok = mbar_wait(bar_q_smem_empty, it & 1, abort_flag, p.err, p.wait_ns);
         if (!ok) break;
         load_q(tile_of(work_of(kn)));
         it++;
       }
       volatile int no_abort = 0;
-      if (lane == 0 && qit > 0) mbar_wait(bar_q_smem_full, (qit - 1) & 1, &no_abort, p.err);
+      if (qit > 0) mbar_wait(bar_q_smem_full, (qit - 1) & 1, &no_abort, p.err);
     }
     __syncwarp();
   } else {
@@ -949,10 +912,18 @@ template <int D, int BK, int NKS, int NVS, int NSB>
 cudaError_t launch_3x_pair(const FwdParams& p, float* ws, int n_split, int num_sms,
                            cudaStream_t s) {
   using C = Tc3PairCfg<D, BK, NKS, NVS, NSB>;
-  // (the lo planes of K and V are formed in shared memory by the kernel)
-  CUtensorMap mkh, mvh, mq;
+  const size_t n = (size_t)p.bh * p.sk * D;  // floats per K (or V) plane
+  float* kl = ws;
+  float* vl = ws + n;
+  split_lo<<<148 * 8, 256, 0, s>>>(reinterpret_cast<const float4*>(p.k),
+                                   reinterpret_cast<const float4*>(p.v),
+                                   reinterpret_cast<float4*>(ws), n / 4);
+  count_launch(1);
+  CUtensorMap mkh, mkl, mvh, mvl, mq;
   if (!make_map(&mkh, p.k, D, p.sk, p.bh, BK / 2, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !make_map(&mkl, kl, D, p.sk, p.bh, BK / 2, CU_TENSOR_MAP_SWIZZLE_128B) ||
       !make_map(&mvh, p.v, D, p.sk, p.bh, BK, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B) ||
+      !make_map(&mvl, vl, D, p.sk, p.bh, BK, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B) ||
       !make_map(&mq, p.q, D, p.sq, p.bh, kBM, CU_TENSOR_MAP_SWIZZLE_128B))
     return cudaErrorInvalidValue;
   static std::atomic<unsigned long long> attr_set{0};
@@ -967,14 +938,14 @@ cudaError_t launch_3x_pair(const FwdParams& p, float* ws, int n_split, int num_s
     attr_set.fetch_or(bit);
   }
   const long long rows = (long long)p.bh * p.sq;
-  float* split_o = n_split > 1 ? ws : nullptr;
+  float* split_o = n_split > 1 ? ws + 2 * n : nullptr;
   float* split_lse = n_split > 1 ? split_o + (size_t)n_split * rows * D : nullptr;
   const int n_pairs = (p.sq + 2 * kBM - 1) / (2 * kBM);
   const long long n_work = (long long)n_pairs * p.bh * n_split;
   if (n_work > INT32_MAX) return cudaErrorInvalidValue;
   const int n_clusters = (int)(n_work < num_sms / 2 ? n_work : num_sms / 2);
   tc_fwd_3xtf32_pair<D, BK, NKS, NVS, NSB><<<dim3(2 * n_clusters), kThreads, C::kSmemBytes, s>>>(
-      mkh, mvh, mq, p, n_pairs, n_split, split_o, split_lse);
+      mkh, mkl, mvh, mvl, mq, p, n_pairs, n_split, split_o, split_lse);
   count_launch();
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess || n_split == 1) return e;
@@ -1073,12 +1044,9 @@ static int tc3_pick_splits(const FwdParams& p, int num_sms) {
 
 size_t tc3_workspace_floats(const FwdParams& p, int num_sms) {
   const int split = tc3_pick_splits(p, num_sms);
-  const bool pair = p.sq > kBM && (p.d == 64 || p.d == 128);
-  // the single-CTA kernel reads the lo planes of K and V from a prepass; the
-  // pair kernel forms them in shared memory
-  size_t f = pair ? 0 : 2 * (size_t)p.bh * p.sk * p.d;
+  size_t f = 2 * (size_t)p.bh * p.sk * p.d;  // lo planes of K and V
   if (split > 1) f += (size_t)split * p.bh * p.sq * (p.d + 1);
-  return f > 16 ? f : 16;
+  return f;
 }
 
 cudaError_t launch_tc3(const FwdParams& p, float* ws, int num_sms, cudaStream_t s) {
