@@ -267,7 +267,10 @@ __global__ void __launch_bounds__(256) decode_fwd(FwdParams p, int chunk, float*
 // Log-sum-exp merge of n partials per row: one warp per row, 8 rows per CTA.
 // The lanes reduce the row's max and sum over the parts, then each lane owns
 // 4 (or 1) output columns and accumulates the parts with weights broadcast by
-// shuffle, 32 parts at a time.
+// shuffle, 32 parts at a time.  With at most 32 parts (every key-range split
+// here) each lane loads its part's LSE once and keeps its weight, and the
+// loads of all parts' columns are issued back to back, so a row costs two
+// dependent memory round trips.
 template <bool V4>
 __global__ void __launch_bounds__(256) lse_combine(const float* __restrict__ o_parts,
                                                    const float* __restrict__ lse_parts,
@@ -277,18 +280,30 @@ __global__ void __launch_bounds__(256) lse_combine(const float* __restrict__ o_p
   const int lane = threadIdx.x & 31;
   const long long row = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
   if (row >= rows) return;  // (whole warps leave together)
-  float M = -INFINITY;
-  for (int p = lane; p < n; p += 32) M = fmaxf(M, lse_parts[(size_t)p * rows + row]);
-  M = warp_max(M);
-  float L = 0.0f;
-  if (M != -INFINITY)
-    for (int p = lane; p < n; p += 32) {
-      const float lp = lse_parts[(size_t)p * rows + row];
-      if (lp != -INFINITY) L += expf(lp - M);
-    }
-  L = warp_sum(L);
-  const float inv_L = L > 0.0f ? 1.0f / L : 0.0f;
   constexpr int W = V4 ? 4 : 1;
+  const float* lrow = lse_parts + row;
+  const size_t pstride = (size_t)rows;  // between parts, in the LSE planes
+  const size_t ostride = (size_t)rows * d;
+  const float* orow = o_parts + (size_t)row * d;
+  float M, L, w_own = 0.0f;
+  if (n <= 32) {
+    const float lp = lane < n ? lrow[(size_t)lane * pstride] : -INFINITY;
+    M = warp_max(lp);
+    w_own = (M != -INFINITY && lp != -INFINITY) ? expf(lp - M) : 0.0f;
+    L = warp_sum(w_own);
+  } else {
+    M = -INFINITY;
+    for (int q = lane; q < n; q += 32) M = fmaxf(M, lrow[(size_t)q * pstride]);
+    M = warp_max(M);
+    L = 0.0f;
+    if (M != -INFINITY)
+      for (int q = lane; q < n; q += 32) {
+        const float lp = lrow[(size_t)q * pstride];
+        if (lp != -INFINITY) L += expf(lp - M);
+      }
+    L = warp_sum(L);
+  }
+  const float inv_L = L > 0.0f ? 1.0f / L : 0.0f;
   for (int c0 = 0; c0 < d; c0 += 32 * W) {
     const int c = c0 + lane * W;
     const bool active = c < d;
@@ -296,24 +311,31 @@ __global__ void __launch_bounds__(256) lse_combine(const float* __restrict__ o_p
 #pragma unroll
     for (int e = 0; e < W; e++) acc[e] = 0.0f;
     for (int p0 = 0; p0 < n && M != -INFINITY; p0 += 32) {
-      float w = 0.0f;
-      if (p0 + lane < n) {
-        const float lp = lse_parts[(size_t)(p0 + lane) * rows + row];
-        if (lp != -INFINITY) w = expf(lp - M);
+      float w = w_own;
+      if (n > 32) {
+        w = 0.0f;
+        if (p0 + lane < n) {
+          const float lp = lrow[(size_t)(p0 + lane) * pstride];
+          if (lp != -INFINITY) w = expf(lp - M);
+        }
       }
       const int cnt = min(32, n - p0);
+#pragma unroll 4
       for (int i = 0; i < cnt; i++) {
         const float wi = __shfl_sync(0xffffffffu, w, i);
-        if (wi == 0.0f || !active) continue;
-        const float* src = o_parts + ((size_t)(p0 + i) * rows + row) * d + c;
+        if (!active) continue;
+        const float* src = orow + (size_t)(p0 + i) * ostride + c;
+        // a part with weight 0 contributes nothing, whatever its columns hold
+        // (a select, not a branch, so the loads of all parts stay in flight)
+        const bool use = wi != 0.0f;
         if constexpr (V4) {
           const float4 o = *reinterpret_cast<const float4*>(src);
-          acc[0] = fmaf(wi, o.x, acc[0]);
-          acc[1] = fmaf(wi, o.y, acc[1]);
-          acc[2] = fmaf(wi, o.z, acc[2]);
-          acc[3] = fmaf(wi, o.w, acc[3]);
+          acc[0] = fmaf(wi, use ? o.x : 0.0f, acc[0]);
+          acc[1] = fmaf(wi, use ? o.y : 0.0f, acc[1]);
+          acc[2] = fmaf(wi, use ? o.z : 0.0f, acc[2]);
+          acc[3] = fmaf(wi, use ? o.w : 0.0f, acc[3]);
         } else {
-          acc[0] = fmaf(wi, *src, acc[0]);
+          acc[0] = fmaf(wi, use ? *src : 0.0f, acc[0]);
         }
       }
     }
