@@ -14,8 +14,43 @@
 #include <thread>
 #include <vector>
 
+#include <immintrin.h>
+
 namespace fa {
 namespace {
+
+// Copy with non-temporal (streaming) stores: the destination lines are written
+// without being read first, which saves a third of the memory traffic of an
+// ordinary copy when many threads copy at once (the staged calls are bound by
+// host memory bandwidth).  AVX2 when the CPU has it, else memcpy.
+__attribute__((target("avx2"))) void copy_stream_avx2(char* dst, const char* src, size_t n) {
+  const size_t head = std::min(n, (size_t)((32 - ((uintptr_t)dst & 31)) & 31));
+  std::memcpy(dst, src, head);
+  dst += head;
+  src += head;
+  n -= head;
+  size_t i = 0;
+  for (; i + 128 <= n; i += 128) {
+    const __m256i a = _mm256_loadu_si256(reinterpret_cast<const __m256i*>(src + i));
+    const __m256i b = _mm256_loadu_si256(reinterpret_cast<const __m256i*>(src + i + 32));
+    const __m256i c = _mm256_loadu_si256(reinterpret_cast<const __m256i*>(src + i + 64));
+    const __m256i d = _mm256_loadu_si256(reinterpret_cast<const __m256i*>(src + i + 96));
+    _mm256_stream_si256(reinterpret_cast<__m256i*>(dst + i), a);
+    _mm256_stream_si256(reinterpret_cast<__m256i*>(dst + i + 32), b);
+    _mm256_stream_si256(reinterpret_cast<__m256i*>(dst + i + 64), c);
+    _mm256_stream_si256(reinterpret_cast<__m256i*>(dst + i + 96), d);
+  }
+  std::memcpy(dst + i, src + i, n - i);
+  _mm_sfence();  // the streamed stores are complete before the copy counts as done
+}
+
+void copy_stream(char* dst, const char* src, size_t n) {
+  static const bool avx2 = __builtin_cpu_supports("avx2");
+  if (avx2 && n >= 4096)
+    copy_stream_avx2(dst, src, n);
+  else
+    std::memcpy(dst, src, n);
+}
 
 // A fixed pool of worker threads for one large memcpy at a time: the caller
 // takes the first part, each worker one of the others.
@@ -36,7 +71,7 @@ class CopyPool {
   }
   void copy(char* dst, const char* src, size_t bytes) {
     if (n_ == 1 || bytes < (size_t(4) << 20)) {
-      std::memcpy(dst, src, bytes);
+      copy_stream(dst, src, bytes);
       return;
     }
     std::lock_guard<std::mutex> call(call_m_);  // one parallel copy at a time
@@ -59,7 +94,7 @@ class CopyPool {
     // 64-byte aligned split points
     const size_t per = ((bytes_ + n_ - 1) / n_ + 63) & ~size_t(63);
     const size_t a = std::min(bytes_, per * i), b = std::min(bytes_, a + per);
-    if (b > a) std::memcpy(dst_ + a, src_ + a, b - a);
+    if (b > a) copy_stream(dst_ + a, src_ + a, b - a);
   }
   void run(int i) {
     unsigned long long seen = 0;
