@@ -400,14 +400,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 // live, so that two S buffers fit in tensor memory and QK^T of the next key
 // block runs while the softmax works on the current one:
 //
-//   Q hi  is the raw Q tile itself, TMA-loaded into this CTA's shared memory
-//         (128 rows x D, 128B swizzle) and read as the A operand of the
-//         hi*hi and hi*lo QK^T MMAs: the tensor core reads it as hi.
-//   Q lo  is written by the softmax warps into tensor memory [0, D) at each
-//         tile change (A operand of the lo*hi MMA).
+//   Q     the raw Q tile is TMA-loaded into this CTA's shared memory (128 rows
+//         x D, 128B swizzle).  At each tile change the softmax warps write Q hi
+//         into tensor memory [0, D) (A operand of the hi*hi and hi*lo MMAs)
+//         and Q lo over the raw tile in place (A operand of the lo*hi MMA, from
+//         shared memory: only one of the three MMAs pays for reading A there).
 //   K, V  raw (hi) and lo planes by TMA; each CTA holds half of every K block
 //         (BK/2 keys) and half of every V block's columns (D/2).
-//   TMEM  Q lo [0, D), O [D, 2D), then NSB buffers of (S / P hi, P lo).
+//   TMEM  Q hi [0, D), O [D, 2D), then NSB buffers of (S / P hi, P lo).
 //
 // Roles (8 warps): warp 0 K producer, warp 1 MMA issuer (leader CTA), warp 2
 // V producer, warp 3 Q loader, warps 4-7 softmax (thread = query row).  The
@@ -557,7 +557,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   cluster_sync_all();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t t_ql = tmem;
+  const uint32_t t_qh = tmem;  // Q hi (A of hi*hi and hi*lo); Q lo lives in shared memory
   const uint32_t t_o = tmem + (uint32_t)D;
   auto t_s = [&](int b) { return tmem + (uint32_t)(2 * D + b * 2 * BK); };  // S / P hi
   auto t_pl = [&](int b) { return tmem + (uint32_t)(2 * D + b * 2 * BK + BK); };
@@ -652,7 +652,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         const int w = work_of(k);
         if (w >= n_work) continue;
         const Tile t = tile_of(w);
-        ok = __all_sync(0xffffffffu, mbar_wait(bar_q_full, it & 1, abort_flag, p.err, p.wait_ns));
+        ok = __all_sync(0xffffffffu, mbar_wait_cl(bar_q_full, it & 1, abort_flag, p.err, p.wait_ns));
         if (!ok) break;
         tc_fence_after();
         for (int j = 0; j < t.n_kv && ok; j++) {
@@ -667,9 +667,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           for (int kk = 0; kk < D / 8; kk++) {
             const uint64_t ko = (uint64_t)(((kk >> 2) * C::kKHalf * 128 + (kk & 3) * 32) >> 4);
             const uint64_t qo = (uint64_t)(((kk >> 2) * kBM * 128 + (kk & 3) * 32) >> 4);
-            mma_ss_pair_elect(t_s(b), qdesc + qo, kh + ko, idesc_qk, kk > 0 ? 1u : 0u);
-            mma_ss_pair_elect(t_s(b), qdesc + qo, kl + ko, idesc_qk, 1u);
-            mma_ts_pair_elect(t_s(b), t_ql + kk * 8, kh + ko, idesc_qk, 1u);
+            // hi*hi and hi*lo with A = Q hi from TMEM, lo*hi with A = Q lo from
+            // shared memory (an SS MMA reads 32 B per row of A and B from shared
+            // memory, a TS one only B's)
+            mma_ts_pair_elect(t_s(b), t_qh + kk * 8, kh + ko, idesc_qk, kk > 0 ? 1u : 0u);
+            mma_ts_pair_elect(t_s(b), t_qh + kk * 8, kl + ko, idesc_qk, 1u);
+            mma_ss_pair_elect(t_s(b), qdesc + qo, kh + ko, idesc_qk, 1u);
           }
           commit_both(bar_s_full(b));
           if (!kKShare) commit_both(bar_k_empty(s));
@@ -777,29 +780,40 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       if (w >= n_work) continue;
       const Tile t = tile_of(w);
       const long long qg = p.q_offset + t.q0 + r;
-      // Q lo of this tile into TMEM.  The previous tile's QK^T MMAs, which read
-      // the old Q lo, have completed: its last S was visible to this warpgroup.
+      // Q hi of this tile into TMEM and Q lo over the raw Q in shared memory
+      // (each thread its own row, in place).  The previous tile's QK^T MMAs,
+      // which read the old Q hi and lo, have completed: its last S was visible
+      // to this warpgroup.
       ok = __all_sync(0xffffffffu, mbar_wait(bar_q_smem_full, it & 1, abort_flag, p.err,
                                              p.wait_ns));
       if (!ok) break;
       {
-        const uint8_t* qrow = smem + C::kOffQ + r * 128;
+        uint8_t* qrow = smem + C::kOffQ + r * 128;
 #pragma unroll
         for (int c = 0; c < D / 32; c++) {
-          uint32_t rl[32];
+          uint32_t rh[32];
 #pragma unroll
           for (int e = 0; e < 8; e++) {
-            const float4 v4 = *reinterpret_cast<const float4*>(
-                qrow + c * (kBM * 128) + ((e ^ (r & 7)) << 4));
+            float4* unit = reinterpret_cast<float4*>(qrow + c * (kBM * 128) + ((e ^ (r & 7)) << 4));
+            const float4 v4 = *unit;
             const float vv[4] = {v4.x, v4.y, v4.z, v4.w};
+            float lo[4];
 #pragma unroll
-            for (int u = 0; u < 4; u++) rl[4 * e + u] = __float_as_uint(vv[u] - hi_part(vv[u]));
+            for (int u = 0; u < 4; u++) {
+              const float h = hi_part(vv[u]);
+              rh[4 * e + u] = __float_as_uint(h);
+              lo[u] = vv[u] - h;
+            }
+            *unit = make_float4(lo[0], lo[1], lo[2], lo[3]);
           }
-          tmem_st32(t_ql + lane_off + c * 32, rl);
+          tmem_st32(t_qh + lane_off + c * 32, rh);
         }
         tmem_wait_st();
+        fence_proxy_async_smem();  // Q lo in shared memory is read by the tensor core
         tc_fence_before();
-        warp_arrive_leader(bar_q_full);
+        // release at cluster scope: the leader's MMAs read this CTA's Q lo
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster_release(at_leader(bar_q_full));
       }
       if (have_prev) epilogue();
       if (!ok) break;

@@ -61,6 +61,49 @@ __device__ __noinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity,
     }
   }
 }
+// Cluster-scope acquire: for barriers whose arrivals come from the peer CTA
+// with release at cluster scope, when the waiter then reads (through the
+// tensor core) shared memory that the arriving threads wrote.
+__device__ __forceinline__ bool mbar_try_wait_cl(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __noinline__ bool mbar_wait_cl_slow(uint32_t bar, uint32_t parity,
+                                               volatile int* abort_flag, int* err,
+                                               unsigned long long limit_ns) {
+  const unsigned long long t0 = globaltimer_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait_cl(bar, parity)) return true;
+    if ((it & 63u) == 0) {
+      if (*abort_flag) return false;
+      if (globaltimer_ns() - t0 > limit_ns) {
+        *abort_flag = 1;
+        atomicExch(err, (int)kErrTimeout);
+        return false;
+      }
+    }
+  }
+}
+__device__ __forceinline__ bool mbar_wait_cl(uint32_t bar, uint32_t parity,
+                                             volatile int* abort_flag, int* err,
+                                             unsigned long long limit_ns) {
+  if (mbar_try_wait_cl(bar, parity)) return true;
+  return mbar_wait_cl_slow(bar, parity, abort_flag, err, limit_ns);
+}
+// Arrive on a barrier that may live in the peer CTA, releasing this thread's
+// earlier writes at cluster scope.
+__device__ __forceinline__ void mbar_arrive_cluster_release(uint32_t cluster_bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar)
+               : "memory");
+}
+
 // The first test inline (the common case: the phase is already complete), the
 // bounded polling loop out of line.
 // Waits that ignore the abort flag (the drains of in-flight copies and MMAs
