@@ -438,6 +438,7 @@ def config_dict(args, cfg, world, h0=None, h1=None):
             "precision": args.precision,
             "parallelism": f"dp{world} (contiguous (batch, head) slice ranges of the fixed "
                            "workload per GPU, no collective)",
+            "host_copy_threads": int(os.environ.get("FA_B200_COPY_THREADS", "0")) or "default",
             "l2": "inputs larger than L2 (no flush)" if bytes_of(bh, sq, sk, d) > 126e6
             else "L2 flushed between steps (256 MB write)"}
 
@@ -538,6 +539,11 @@ def main():
     if args.impl == "reference":
         return run_reference(args)
 
+    # One process per GPU shares the host: each rank's copy pool (the staged
+    # host-slice calls) gets its share of the cores.
+    world_env = int(os.environ.get("WORLD_SIZE", "1"))
+    if world_env > 1 and "FA_B200_COPY_THREADS" not in os.environ:
+        os.environ["FA_B200_COPY_THREADS"] = str(max(2, (os.cpu_count() or 16) // world_env))
     import numpy as np
     import torch
     import torch.distributed as dist

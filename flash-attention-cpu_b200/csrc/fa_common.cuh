@@ -138,5 +138,12 @@ size_t bwd_workspace_floats(const BwdParams& p);
 // bwd_workspace_floats(p) floats.
 cudaError_t launch_bwd(BwdParams p, float* dvec, cudaStream_t s);
 cudaError_t staging_acquire(int dev, PinnedRing** in, PinnedRing** out, std::mutex** call);
+// One copy between host memory and device `dev` (current), enqueued on `s`.
+// Pageable host memory goes through the device's pinned rings with the copy
+// pool; page-locked memory is copied directly.  staged_copy_h2d returns once
+// every piece is handed to the copy engine (the source may then be reused);
+// staged_copy_d2h returns once `dst` holds the data.
+cudaError_t staged_copy_h2d(int dev, void* dst, const void* src, size_t bytes, cudaStream_t s);
+cudaError_t staged_copy_d2h(int dev, void* dst, const void* src, size_t bytes, cudaStream_t s);
 void staging_release_all();
 }  // namespace fa

@@ -308,15 +308,14 @@ int kv_split_slice(const int* devs, int n, const float* q, const float* k, const
     float* ws = K.ws;
     cudaError_t e = cudaSuccess;
     if (z.any) {
-      e = cudaMemcpyAsync(ws + z.q, q + z.qrow0 * d, (sq - z.qrow0) * d * sizeof(float),
-                          cudaMemcpyHostToDevice, K.s);
+      // (pageable host memory goes through the device's pinned rings)
+      e = staged_copy_h2d(dev, ws + z.q, q + z.qrow0 * d, (sq - z.qrow0) * d * sizeof(float), K.s);
       for (int c = 0; c < P.nch && e == cudaSuccess; c++) {
         const Plan::Chunk& x = P.ch[c];
         if (!x.used || x.slot != s) continue;
         const size_t nb = (x.k1 - x.k0) * d * sizeof(float);
-        e = cudaMemcpyAsync(ws + z.k + x.kv_off, k + x.k0 * d, nb, cudaMemcpyHostToDevice, K.s);
-        if (e == cudaSuccess)
-          e = cudaMemcpyAsync(ws + z.v + x.kv_off, v + x.k0 * d, nb, cudaMemcpyHostToDevice, K.s);
+        e = staged_copy_h2d(dev, ws + z.k + x.kv_off, k + x.k0 * d, nb, K.s);
+        if (e == cudaSuccess) e = staged_copy_h2d(dev, ws + z.v + x.kv_off, v + x.k0 * d, nb, K.s);
       }
       if (e != cudaSuccess) return fail(s, status_cuda(e, "key-range split inputs"));
       for (int c = 0; c < P.nch; c++) {
@@ -386,11 +385,9 @@ int kv_split_slice(const int* devs, int n, const float* q, const float* k, const
       e = launch_combine(K.ws + y.recv, K.ws + y.recv + up16(np * len * d), (int)np,
                          (long long)len, (int)d, K.ws + y.out, K.ws + y.lse, K.s);
       if (e == cudaSuccess)
-        e = cudaMemcpyAsync(out + y.r0 * d, K.ws + y.out, len * d * sizeof(float),
-                            cudaMemcpyDeviceToHost, K.s);
+        e = staged_copy_d2h(dev, out + y.r0 * d, K.ws + y.out, len * d * sizeof(float), K.s);
       if (e == cudaSuccess && lse)
-        e = cudaMemcpyAsync(lse + y.r0, K.ws + y.lse, len * sizeof(float), cudaMemcpyDeviceToHost,
-                            K.s);
+        e = staged_copy_d2h(dev, lse + y.r0, K.ws + y.lse, len * sizeof(float), K.s);
     }
     if (e != cudaSuccess) {
       cudaStreamSynchronize(K.s);

@@ -8,6 +8,7 @@
 #include "fa_common.cuh"
 
 #include <algorithm>
+#include <cstdlib>
 #include <condition_variable>
 #include <cstring>
 #include <mutex>
@@ -53,12 +54,18 @@ void copy_stream(char* dst, const char* src, size_t n) {
 }
 
 // A fixed pool of worker threads for one large memcpy at a time: the caller
-// takes the first part, each worker one of the others.
+// takes the first part, each worker one of the others.  Up to 16 threads, one
+// per hardware thread; FA_B200_COPY_THREADS (read once) sets the count, for
+// processes that share a host (one process per GPU: divide the cores).
 class CopyPool {
  public:
   CopyPool() {
     const unsigned hw = std::thread::hardware_concurrency();
     n_ = (int)std::min(16u, std::max(1u, hw));
+    if (const char* e = std::getenv("FA_B200_COPY_THREADS")) {
+      const int v = std::atoi(e);
+      if (v >= 1 && v <= 64) n_ = v;
+    }
     for (int i = 1; i < n_; i++) workers_.emplace_back([this, i] { run(i); });
   }
   ~CopyPool() {
@@ -204,6 +211,78 @@ cudaError_t staging_acquire(int dev, PinnedRing** in, PinnedRing** out, std::mut
   *in = &g.in;
   *out = &g.out;
   return cudaSuccess;
+}
+
+cudaError_t staged_copy_h2d(int dev, void* dst, const void* src, size_t bytes, cudaStream_t s) {
+  if (!is_pageable(src)) return cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, s);
+  PinnedRing *rin = nullptr, *rout = nullptr;
+  std::mutex* call = nullptr;
+  cudaError_t e = staging_acquire(dev, &rin, &rout, &call);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> unlock(*call, std::adopt_lock);
+  constexpr size_t kSlot = PinnedRing::kSlotBytes;
+  for (size_t off = 0; off < bytes && e == cudaSuccess; off += kSlot) {
+    const size_t n = std::min(kSlot, bytes - off);
+    const int sl = rin->next;
+    rin->next = (sl + 1) % PinnedRing::kSlots;
+    if (rin->busy[sl] && (e = cudaEventSynchronize(rin->ev[sl])) != cudaSuccess) break;
+    parallel_copy(rin->buf[sl], static_cast<const char*>(src) + off, n);
+    e = cudaMemcpyAsync(static_cast<char*>(dst) + off, rin->buf[sl], n, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) e = cudaEventRecord(rin->ev[sl], s);
+    rin->busy[sl] = e == cudaSuccess;
+  }
+  return e;
+}
+
+cudaError_t staged_copy_d2h(int dev, void* dst, const void* src, size_t bytes, cudaStream_t s) {
+  if (!is_pageable(dst)) {
+    cudaError_t e = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, s);
+    return e == cudaSuccess ? cudaStreamSynchronize(s) : e;
+  }
+  PinnedRing *rin = nullptr, *rout = nullptr;
+  std::mutex* call = nullptr;
+  cudaError_t e = staging_acquire(dev, &rin, &rout, &call);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> unlock(*call, std::adopt_lock);
+  constexpr size_t kSlot = PinnedRing::kSlotBytes;
+  struct Piece {
+    int slot;
+    size_t off, n;
+  };
+  std::vector<Piece> pend;  // pieces in flight, oldest first
+  size_t head = 0;
+  auto drain_one = [&]() -> cudaError_t {
+    const Piece pc = pend[head++];
+    cudaError_t r = cudaEventSynchronize(rout->ev[pc.slot]);
+    if (r == cudaSuccess) parallel_copy(static_cast<char*>(dst) + pc.off, rout->buf[pc.slot], pc.n);
+    rout->busy[pc.slot] = false;
+    return r;
+  };
+  for (size_t off = 0; off < bytes && e == cudaSuccess; off += kSlot) {
+    const size_t n = std::min(kSlot, bytes - off);
+    const int sl = rout->next;
+    rout->next = (sl + 1) % PinnedRing::kSlots;
+    while (e == cudaSuccess && rout->busy[sl]) {
+      if (head < pend.size()) {
+        e = drain_one();
+      } else {  // (a slot left busy by an earlier call: wait for its copy)
+        e = cudaEventSynchronize(rout->ev[sl]);
+        rout->busy[sl] = false;
+      }
+    }
+    if (e != cudaSuccess) break;
+    e = cudaMemcpyAsync(rout->buf[sl], static_cast<const char*>(src) + off, n,
+                        cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaEventRecord(rout->ev[sl], s);
+    if (e != cudaSuccess) break;
+    rout->busy[sl] = true;
+    pend.push_back({sl, off, n});
+  }
+  while (head < pend.size()) {
+    cudaError_t r = drain_one();
+    if (e == cudaSuccess) e = r;
+  }
+  return e;
 }
 
 void staging_release_all() {

@@ -88,18 +88,24 @@ def test_c5_over_listed_devices_matches_one_device(fa):
     assert max_abs_diff(lse, wlse) < 2e-3
 
 
-def test_several_gpus(fa):
+@pytest.mark.parametrize("prec", [0, 1])
+def test_several_gpus(fa, prec):
     # Distinct GPUs (peer copies between devices), where the box has them.
+    # Checked against the oracle: the one-device result is itself a TF32
+    # approximation, so two such results may differ by twice the tolerance.
     n = fa.device_count()
     if n < 2:
         pytest.skip("one GPU")
     devs = list(range(min(n, 8)))
-    fa.set_precision(0)
+    fa.set_precision(prec)
     for bh, sq, sk, d, causal in ((32, 2048, 2048, 128, True), (1, 32768, 32768, 128, True)):
         q, k, v = (random_vec(bh * sq * d, 21), random_vec(bh * sk * d, 22),
                    random_vec(bh * sk * d, 23))
-        want, wlse = _one_device(fa, q, k, v, bh, sq, sk, d, causal)
         fa.set_devices(devs)
         out, lse = fa.multihead_lse(q, k, v, bh, sq, sk, d, causal)
-        assert max_abs_diff(out, want) < 2e-3
-        assert max_abs_diff(lse, wlse) < 2e-3
+        nb = (sq + 63) // 64
+        items = sorted({h * nb + b for h in {0, bh - 1} for b in (0, 1, nb // 2, nb - 2, nb - 1)})
+        want, wlse = O.flash_v2_items(q, k, v, bh, sq, sk, d, causal, items)
+        rows = O.item_rows(items, sq)
+        assert max_abs_diff(out.reshape(-1, d)[rows], want.reshape(-1, d)[rows]) < TOL[prec]
+        assert max_abs_diff(lse[rows], wlse[rows]) < TOL[prec]
