@@ -622,15 +622,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         tc_commit_pair_elect(at_peer(bar));
       };
       const uint64_t qdesc = smem_desc(sQ, 16, 1024, kLayoutSw128);
-      // PV of global block G (block j of its tile): O (+)= P(G) V(G), three terms
-      auto issue_pv = [&](int G, int j) -> bool {
-        const int b = G % NSB, sv = G % NVS;
-        if (!__all_sync(0xffffffffu, mbar_wait(bar_p_full(b), (G / NSB) & 1, abort_flag, p.err,
-                                               p.wait_ns)))
-          return false;
-        if (!__all_sync(0xffffffffu, mbar_wait(bar_v_full(sv), (G / NVS) & 1, abort_flag, p.err,
-                                               p.wait_ns)))
-          return false;
+      // K(G) known to have landed (checked while waiting for an earlier P)
+      bool k_known = false;
+      // PV of global block G (block j of its tile): O (+)= P(G) V(G), three
+      // terms.  While waiting for P(G) it also checks V(G) and, when poll_k,
+      // K(G + 2), the block of the next QK^T.
+      auto issue_pv = [&](int G, int j, bool poll_k) -> bool {
+        const int b = G % NSB, sv = G % NVS, gk = G + 2;
+        bool kd = false;
+        const bool w = mbar_wait2_poll(bar_p_full(b), (G / NSB) & 1, bar_v_full(sv), (G / NVS) & 1,
+                                       bar_k_full(gk % NKS), (gk / NKS) & 1, poll_k, &kd,
+                                       abort_flag, p.err, p.wait_ns);
+        if (!__all_sync(0xffffffffu, w)) return false;
+        k_known = __all_sync(0xffffffffu, kd);
         tc_fence_after();
         const uint64_t vh =
             smem_desc(sV + sv * 2 * C::kVPlane, BK * 128, 512, kLayoutSw128Base32);
@@ -657,8 +661,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         tc_fence_after();
         for (int j = 0; j < t.n_kv && ok; j++) {
           const int Gj = G + j, s = Gj % NKS, b = Gj % NSB;
-          ok = __all_sync(0xffffffffu, mbar_wait(bar_k_full(s), (Gj / NKS) & 1, abort_flag, p.err,
-                                                 p.wait_ns));
+          if (!k_known)
+            ok = __all_sync(0xffffffffu, mbar_wait(bar_k_full(s), (Gj / NKS) & 1, abort_flag, p.err,
+                                                   p.wait_ns));
+          k_known = false;
           if (!ok) break;
           tc_fence_after();
           const uint64_t kh = smem_desc(sK + s * 2 * C::kKPlane, 16, 1024, kLayoutSw128);
@@ -677,11 +683,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           commit_both(bar_s_full(b));
           if (!kKShare) commit_both(bar_k_empty(s));
           if (j == t.n_kv - 1) commit_both(bar_q_smem_empty);  // the tile's last QK^T
-          if (j > 0) ok = issue_pv(Gj - 1, j - 1);
+          // (the next QK^T is S(Gj + 1) = block (Gj - 1) + 2, in this tile if j + 1 < n_kv)
+          if (j > 0) ok = issue_pv(Gj - 1, j - 1, j + 1 < t.n_kv);
         }
         if (!ok) break;
         if (t.n_kv == 0) commit_both(bar_q_smem_empty);
-        if (t.n_kv > 0) ok = issue_pv(G + t.n_kv - 1, t.n_kv - 1);
+        if (t.n_kv > 0) ok = issue_pv(G + t.n_kv - 1, t.n_kv - 1, false);
+        k_known = false;
         if (!ok) break;
         commit_both(bar_o_final);
         G += t.n_kv;

@@ -61,6 +61,45 @@ __device__ __noinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity,
     }
   }
 }
+// Waits (bounded, as mbar_wait) until barriers a and b have completed the
+// given phases, and polls barrier c alongside when poll_c: *c_done says
+// whether c had completed by then.  The checks of b and c overlap the wait for
+// a instead of following it (a check of a ready barrier still costs ~100+
+// cycles, time in which the MMA warp queues nothing).
+__device__ __noinline__ bool mbar_wait2_poll_slow(uint32_t a, uint32_t pa, uint32_t b, uint32_t pb,
+                                                  uint32_t c, uint32_t pc, bool da, bool db,
+                                                  bool* dc, volatile int* abort_flag, int* err,
+                                                  unsigned long long limit_ns) {
+  const unsigned long long t0 = globaltimer_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (!da) da = mbar_try_wait(a, pa);
+    if (!db) db = mbar_try_wait(b, pb);
+    if (!*dc) *dc = mbar_try_wait(c, pc);
+    if (da && db) return true;
+    if ((it & 63u) == 0) {
+      if (*abort_flag) return false;
+      if (globaltimer_ns() - t0 > limit_ns) {
+        *abort_flag = 1;
+        atomicExch(err, (int)kErrTimeout);
+        return false;
+      }
+    }
+  }
+}
+__device__ __forceinline__ bool mbar_wait2_poll(uint32_t a, uint32_t pa, uint32_t b, uint32_t pb,
+                                                uint32_t c, uint32_t pc, bool poll_c, bool* c_done,
+                                                volatile int* abort_flag, int* err,
+                                                unsigned long long limit_ns) {
+  const bool da = mbar_try_wait(a, pa);
+  const bool db = mbar_try_wait(b, pb);
+  bool dc = !poll_c || mbar_try_wait(c, pc);
+  bool ok = true;
+  if (!(da && db)) ok = mbar_wait2_poll_slow(a, pa, b, pb, c, pc, da, db, &dc, abort_flag, err,
+                                             limit_ns);
+  *c_done = poll_c && dc;
+  return ok;
+}
+
 // Cluster-scope acquire: for barriers whose arrivals come from the peer CTA
 // with release at cluster scope, when the waiter then reads (through the
 // tensor core) shared memory that the arriving threads wrote.
