@@ -543,7 +543,11 @@ def main():
     # host-slice calls) gets its share of the cores.
     world_env = int(os.environ.get("WORLD_SIZE", "1"))
     if world_env > 1 and "FA_B200_COPY_THREADS" not in os.environ:
-        os.environ["FA_B200_COPY_THREADS"] = str(max(2, (os.cpu_count() or 16) // world_env))
+        try:
+            cores = len(os.sched_getaffinity(0))  # the CPUs this process may run on
+        except AttributeError:
+            cores = os.cpu_count() or 16
+        os.environ["FA_B200_COPY_THREADS"] = str(max(2, min(16, cores // world_env)))
     import numpy as np
     import torch
     import torch.distributed as dist
