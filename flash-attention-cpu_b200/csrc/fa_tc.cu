@@ -82,33 +82,6 @@ struct TcCfg {
   static_assert(kSmemBytes <= 232448, "shared-memory budget");
 };
 
-// ---- optional cycle trace (diagnostic builds only, -DFA_TRACE) -------------
-#ifdef FA_TRACE
-__device__ unsigned long long g_fa_trace[32];
-#define FA_TR_T0() long long tr_t0 = clock64()
-#define FA_TR_ADD(slot) atomicAdd(&g_fa_trace[slot], (unsigned long long)(clock64() - tr_t0))
-#define FA_TR_CNT(slot) atomicAdd(&g_fa_trace[slot], 1ull)
-// per-tile event timestamps of one CTA pair (blockIdx.y == 0, blockIdx.z == 0)
-// (CTAs 0 and 1 of the first cluster: [cta][kind][block]; clock64 of each SM)
-__device__ long long g_fa_events[2][24][256];
-#define FA_EV(kind, j)                                                              \
-  if (blockIdx.y == 0 && blockIdx.z == 0 && blockIdx.x < 2 && (j) < 256)            \
-  g_fa_events[blockIdx.x][kind][j] = clock64()
-#else
-#define FA_EV(kind, j) \
-  do {                 \
-  } while (0)
-#define FA_TR_T0() \
-  do {             \
-  } while (0)
-#define FA_TR_ADD(slot) \
-  do {                  \
-  } while (0)
-#define FA_TR_CNT(slot) \
-  do {                  \
-  } while (0)
-#endif
-
 // ---- the kernel ------------------------------------------------------------
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
   float r;
@@ -149,9 +122,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kOffBar + C::kNumBars * 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
-#ifdef FA_TRACE
-  const long long tr_kstart = clock64();
-#endif
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int bh = blockIdx.x;
   const int n_qt = gridDim.y;
@@ -215,11 +185,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (int j = 0; j < n_kv && ok; j++) {
         const int sk = j % NKS;
-        {
-          FA_TR_T0();
-          if (j >= NKS) ok = mbar_wait(bar_k_empty(sk), ((j / NKS) & 1) ^ 1, abort_flag, p.err, p.wait_ns);
-          FA_TR_ADD(0);
-        }
+        if (j >= NKS) ok = mbar_wait(bar_k_empty(sk), ((j / NKS) & 1) ^ 1, abort_flag, p.err, p.wait_ns);
         if (!ok) break;
         mbar_expect_tx(bar_k_full(sk), C::kKBytes);
         for (int c = 0; c < C::kChunks; c++)
@@ -243,11 +209,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int n_v = n_kv * VS;
       for (int g = 0; g < n_v && ok; g++) {
         const int sv = g % NVS;
-        {
-          FA_TR_T0();
-          if (g >= NVS) ok = mbar_wait(bar_v_empty(sv), ((g / NVS) & 1) ^ 1, abort_flag, p.err, p.wait_ns);
-          FA_TR_ADD(1);
-        }
+        if (g >= NVS) ok = mbar_wait(bar_v_empty(sv), ((g / NVS) & 1) ^ 1, abort_flag, p.err, p.wait_ns);
         if (!ok) break;
         mbar_expect_tx(bar_v_full(sv), C::kVBytes);
         for (int c = 0; c < C::kChunks; c++)
@@ -269,21 +231,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       auto issue_pv = [&](int jj) -> bool {
         const int b = jj & 1;
-        {
-          FA_TR_T0();
-          if (!__all_sync(0xffffffffu, mbar_wait(bar_p_full(b), (jj >> 1) & 1, abort_flag, p.err, p.wait_ns)))
-            return false;
-          if (lane == 0) FA_TR_ADD(3);
-        }
+        if (!__all_sync(0xffffffffu, mbar_wait(bar_p_full(b), (jj >> 1) & 1, abort_flag, p.err, p.wait_ns)))
+          return false;
 #pragma unroll
         for (int h = 0; h < VS; h++) {
           const int g = jj * VS + h, sv = g % NVS;
-          {
-            FA_TR_T0();
-            if (!__all_sync(0xffffffffu, mbar_wait(bar_v_full(sv), (g / NVS) & 1, abort_flag, p.err, p.wait_ns)))
-              return false;
-            if (lane == 0) FA_TR_ADD(4);
-          }
+          if (!__all_sync(0xffffffffu, mbar_wait(bar_v_full(sv), (g / NVS) & 1, abort_flag, p.err, p.wait_ns)))
+            return false;
           tc_fence_after();
           // 8 keys = two 4-row groups (SBO = 512 B); 32-column chunks LBO apart
           const uint64_t vdesc =
@@ -299,11 +253,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       };
       for (int j = 0; j < n_kv && ok; j++) {
         const int s = j % NKS, b = j & 1;
-        {
-          FA_TR_T0();
-          ok = __all_sync(0xffffffffu, mbar_wait(bar_k_full(s), (j / NKS) & 1, abort_flag, p.err, p.wait_ns));
-          if (lane == 0) FA_TR_ADD(2);
-        }
+        ok = __all_sync(0xffffffffu, mbar_wait(bar_k_full(s), (j / NKS) & 1, abort_flag, p.err, p.wait_ns));
         if (!ok) break;
         tc_fence_after();
         const uint64_t kdesc = smem_desc(sK + s * C::kKBytes, 16, 1024, kLayoutSw128);
@@ -357,13 +307,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     float l = 0.0f;
     for (int j = 0; j < n_kv && ok; j++) {
       const int b = j & 1;
-      {
-        FA_TR_T0();
-        ok = __all_sync(0xffffffffu, mbar_wait(bar_s_full(b), (j >> 1) & 1, abort_flag, p.err, p.wait_ns));
-        if (threadIdx.x == 128) FA_TR_ADD(5);
-      }
+      ok = __all_sync(0xffffffffu, mbar_wait(bar_s_full(b), (j >> 1) & 1, abort_flag, p.err, p.wait_ns));
       if (!ok) break;
-      FA_TR_T0();
       tc_fence_after();
       float x[BK];
       {
@@ -405,7 +350,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         m = m_new;
       }
       if (__any_sync(0xffffffffu, need)) {
-        if (threadIdx.x == 128) FA_TR_CNT(7);
         // O is being accumulated by PV_{j-1}: wait for it, then rescale in TMEM.
         ok = __all_sync(0xffffffffu, mbar_wait(bar_o_done, (j - 1) & 1, abort_flag, p.err, p.wait_ns));
         if (!ok) break;
@@ -452,10 +396,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!(p.test_skip == j && threadIdx.x == 128 && blockIdx.x == 0 && blockIdx.y == 0 &&
             blockIdx.z == 0))
         mbar_arrive(bar_p_full(b));
-      if (threadIdx.x == 128) {
-        FA_TR_ADD(6);
-        FA_TR_CNT(8);
-      }
     }
     // epilogue: out = O / l, lse = ln(sum exp(s)) = (m + log2 l) * ln 2
     if (n_kv > 0) {
@@ -494,12 +434,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_before();
   }
   __syncthreads();
-#ifdef FA_TRACE
-  if (threadIdx.x == 0) {
-    atomicAdd(&g_fa_trace[9], (unsigned long long)(clock64() - tr_kstart));
-    atomicAdd(&g_fa_trace[10], 1ull);
-  }
-#endif
   if (warp == 1) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
@@ -731,7 +665,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(NG), 1)
             ok = mbar_wait(empty, ((G / NS) & 1) ^ 1, abort_flag, p.err, p.wait_ns);
           }
           if (!ok) break;
-          FA_EV(is_k ? 12 : 11, G);
           const uint32_t full = at_leader(is_k ? bar_k_full(s) : bar_v_full(s));
           if (is_k) {
             mbar_expect_tx_cluster(full, C::kKBytes);
@@ -771,10 +704,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(NG), 1)
         const int b = G & 1, sv = G % NVS;
         if (!__all_sync(0xffffffffu, mbar_wait(bar_p_full(b), (G >> 1) & 1, abort_flag, p.err, p.wait_ns)))
           return false;
-        if (lane == 0) FA_EV(2, G);
         if (!__all_sync(0xffffffffu, mbar_wait(bar_v_full(sv), (G / NVS) & 1, abort_flag, p.err, p.wait_ns)))
           return false;
-        if (lane == 0) FA_EV(3, G);
         tc_fence_after();
         // 8 keys per MMA = two 4-row groups (SBO = 512 B); 32-column chunks LBO apart
         const uint64_t vdesc = smem_desc(sV + sv * C::kVBytes, BK * 128, 512, kLayoutSw128Base32);
@@ -784,7 +715,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(NG), 1)
                             (j > 0 || kk > 0) ? 1u : 0u);
         if (!kVShare) commit_both(bar_v_empty(sv));
         commit_both(bar_o_done(G & 1));
-        if (lane == 0) FA_EV(4, G);
         return true;
       };
       bool ok = true;
@@ -798,10 +728,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(NG), 1)
         tc_fence_after();
         for (int j = 0; j < t.n_kv && ok; j++) {
           const int Gj = G + j, s = Gj % NKS, b = Gj & 1;
-          if (lane == 0) FA_EV(13, Gj);
           ok = __all_sync(0xffffffffu, mbar_wait(bar_k_full(s), (Gj / NKS) & 1, abort_flag, p.err, p.wait_ns));
           if (!ok) break;
-          if (lane == 0) FA_EV(0, Gj);
           tc_fence_after();
           const uint64_t kdesc = smem_desc(sK + s * C::kKBytes, 16, 1024, kLayoutSw128);
 #pragma unroll
@@ -811,7 +739,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(NG), 1)
                               idesc_qk, kk > 0 ? 1u : 0u);
           commit_both(bar_s_full(b));
           if (!kKShare) commit_both(bar_k_empty(s));
-          if (lane == 0) FA_EV(1, Gj);
           if (j > 0) ok = issue_pv(Gj - 1, j - 1);
         }
         if (ok && t.n_kv > 0) ok = issue_pv(G + t.n_kv - 1, t.n_kv - 1);
@@ -846,7 +773,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(NG), 1)
       // This CTA's 128 rows of a tile's Q, as D/32 swizzled [128 x 32] chunks
       // (rows past the slice read as zeros).
       auto load_q = [&](const Tile& q) {
-        FA_EV(19, qit);
         mbar_expect_tx(bar_q_smem_full, C::kQBytes);
         for (int c = 0; c < D / 32; c++)
           tma_load_3d(sQ + c * (kBM * 128), &tmQ, bar_q_smem_full, 32 * c, q.q0, q.bh);
@@ -864,7 +790,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(NG), 1)
         ok = mbar_wait(bar_o_smem_full, it & 1, abort_flag, p.err, p.wait_ns);
         if (!ok) break;
         if (have_prev) store(false);
-        FA_EV(18, it);
         const int kn = next_work(k);
         if (kn >= 0) load_q(tile_of(work_of(kn)));
         have_prev = true;
@@ -967,10 +892,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(NG), 1)
       // Stage this tile's Q from the shared-memory buffer.  The previous tile's
       // QK^T MMAs are complete: its last S was visible before its last P was
       // written.
-      if (lane == 0 && quarter == 0 && g == 0) FA_EV(17, G);
       const bool okq =
           ok && __all_sync(0xffffffffu, mbar_wait(bar_q_smem_full, it & 1, abort_flag, p.err, p.wait_ns));
-      if (lane == 0 && quarter == 0 && g == 0) FA_EV(14, G);
       if (okq) {
 #pragma unroll
         for (int c = 0; c < HD / CW; c++) {
@@ -991,10 +914,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(NG), 1)
         tc_fence_before();
         warp_arrive_leader(bar_q_full);
       }
-      if (lane == 0 && quarter == 0 && g == 0) FA_EV(15, G);
       float l_prev = 0.0f;
       const bool oke = have_prev ? epilogue_smem(okq, &l_prev) : okq;
-      if (lane == 0 && quarter == 0 && g == 0) FA_EV(16, G);
       if (!oke) ok = false;
       if (ok) {
         // this warp's O rows (if any) reach the TMA store through warp 3
@@ -1010,7 +931,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(NG), 1)
         const int Gj = G + j, b = Gj & 1;
         const bool wt =
             __all_sync(0xffffffffu, mbar_wait(bar_s_full(b), (Gj >> 1) & 1, abort_flag, p.err, p.wait_ns));
-        if (lane == 0 && quarter == 0 && g < 2) FA_EV(5 + 3 * g, Gj);
         tc_fence_after();
         float x[HC];
         if (wt) {
@@ -1054,7 +974,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(NG), 1)
           ok = false;
           break;
         }
-        if (lane == 0 && quarter == 0 && g < 2) FA_EV(6 + 3 * g, Gj);
         float mx_row = mx_half;
 #pragma unroll
         for (int i = 0; i < NG; i++) mx_row = fmaxf(mx_row, slot[i * 128 + r]);
@@ -1119,9 +1038,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(NG), 1)
         // withholds its arrive)
         if (!(p.test_skip == Gj && blockIdx.x == 0 && warp == kSoftmaxWarp0))
           warp_arrive_leader(bar_p_full(b));
-        if (lane == 0 && quarter == 0 && g < 2) FA_EV(7 + 3 * g, Gj);
       }
-      if (lane == 0 && quarter == 0 && g == 0) FA_EV(20, G);
       G += t.n_kv;
       have_prev = true;
       pt = t;
@@ -1234,18 +1151,6 @@ cudaError_t launch_tf32_pair(const FwdParams& p, cudaStream_t s, int n_split = 1
 
 }  // namespace
 
-#ifdef FA_TRACE
-extern "C" __attribute__((visibility("default"))) int fa_events_read(long long* out) {
-  cudaDeviceSynchronize();
-  return (int)cudaMemcpyFromSymbol(out, g_fa_events, sizeof(g_fa_events));
-}
-extern "C" __attribute__((visibility("default"))) int fa_trace_read(unsigned long long* out) {
-  cudaDeviceSynchronize();
-  cudaMemcpyFromSymbol(out, g_fa_trace, sizeof(g_fa_trace));
-  unsigned long long z[32] = {0};
-  return (int)cudaMemcpyToSymbol(g_fa_trace, z, sizeof(z));
-}
-#endif
 
 // d = 64, 128: the CTA-pair kernel (more than 128 query rows) and the
 // single-CTA kernel; d = 32, 96: the single-CTA kernel at every length (the
