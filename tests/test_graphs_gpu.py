@@ -21,13 +21,17 @@ TOL = {0: 2e-3, 1: 2e-5, 2: 2e-5}
 
 # (bh, sq, sk, d, causal, precision): the pair kernel with and without
 # key-range parts, the single-CTA kernel with parts, split-KV decode, the
-# 3xTF32 kernel with parts, and the CUDA-core f32 kernel.
+# 3xTF32 pair kernel with and without parts (its split_lo prepass included),
+# the single-CTA kernels at d = 32 and 96, and the CUDA-core f32 kernel.
 CASES = [
     (2, 512, 512, 128, True, 0),
     (1, 1024, 4096, 128, False, 0),
     (1, 100, 8192, 128, False, 0),
     (4, 1, 8192, 128, False, 0),
     (1, 512, 4096, 64, True, 1),
+    (12, 1024, 1024, 128, True, 1),
+    (2, 300, 700, 96, False, 1),
+    (2, 300, 300, 32, True, 0),
     (2, 200, 300, 96, True, 2),
 ]
 
