@@ -63,6 +63,19 @@ __device__ __forceinline__ unsigned long long globaltimer_ns() {
   return t;
 }
 
+// Programmatic dependent launch: kernels launched with launch_pdl may start
+// while the previous kernel on the stream is finishing.  Each such kernel does
+// its set-up (barrier init, tensor-memory allocation) and then calls
+// grid_dep_wait() before it touches global memory, which waits until the
+// previous grid has completed and its writes are visible.  grid_dep_launch()
+// lets the next kernel be scheduled early (it still waits in grid_dep_wait).
+__device__ __forceinline__ void grid_dep_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void grid_dep_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 __device__ __forceinline__ float warp_max(float x) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, o));
@@ -79,6 +92,25 @@ __device__ __forceinline__ float warp_sum(float x) {
 __host__ __device__ __forceinline__ int causal_limit(long long qg, long long kg0, int n) {
   long long lim = qg - kg0 + 1;
   return lim < 0 ? 0 : (lim > n ? n : (int)lim);
+}
+
+// Launch with the programmatic-stream-serialization attribute (see
+// grid_dep_wait): the kernel must call grid_dep_wait() before it reads or
+// writes global memory that earlier work on the stream produces or uses.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t s, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
 }
 
 }  // namespace fa

@@ -277,6 +277,7 @@ __global__ void __launch_bounds__(256) lse_combine(const float* __restrict__ o_p
                                                    int n, long long rows, int d,
                                                    float* __restrict__ out,
                                                    float* __restrict__ lse_out) {
+  grid_dep_wait();  // (launched with launch_pdl: the partials come from the previous kernel)
   const int lane = threadIdx.x & 31;
   const long long row = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
   if (row >= rows) return;  // (whole warps leave together)
@@ -456,12 +457,13 @@ cudaError_t launch_combine(const float* o_parts, const float* lse_parts, int n_p
   if (rows <= 0) return cudaSuccess;
   const unsigned grid = (unsigned)((rows + 7) / 8);
   const bool v4 = (d % 4) == 0 && (((uintptr_t)o_parts | (uintptr_t)out) & 15) == 0;
-  if (v4)
-    lse_combine<true><<<grid, 256, 0, s>>>(o_parts, lse_parts, n_parts, rows, d, out, lse_out);
-  else
-    lse_combine<false><<<grid, 256, 0, s>>>(o_parts, lse_parts, n_parts, rows, d, out, lse_out);
+  cudaError_t e =
+      v4 ? launch_pdl(lse_combine<true>, dim3(grid), dim3(256), 0, s, o_parts, lse_parts, n_parts,
+                      rows, d, out, lse_out)
+         : launch_pdl(lse_combine<false>, dim3(grid), dim3(256), 0, s, o_parts, lse_parts, n_parts,
+                      rows, d, out, lse_out);
   count_launch();
-  return cudaGetLastError();
+  return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 // ---------------------------------------------------------------------------

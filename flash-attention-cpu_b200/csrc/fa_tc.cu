@@ -156,7 +156,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(bar_o_done, 1);
     mbar_init(bar_drain, 1);
     mbar_init(bar_o_final, 1);
-    *abort_flag = (*(volatile int*)p.err != 0) ? 1 : 0;  // an earlier CTA failed: skip work
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   }
@@ -167,6 +166,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
+  // (the set-up above overlaps the previous kernel on the stream; global
+  // memory is touched only after it has completed)
+  grid_dep_wait();
+  if (threadIdx.x == 0) *abort_flag = (*(volatile int*)p.err != 0) ? 1 : 0;  // an earlier CTA failed: skip work
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -627,7 +630,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(NG), 1)
     mbar_init(bar_o_final, 1);
     mbar_init(bar_q_smem_full, 1);  // warp 3
     mbar_init(bar_o_smem_full, 4 * NG);  // the softmax warps of this CTA
-    *abort_flag = (*(volatile int*)p.err != 0) ? 1 : 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
@@ -637,6 +639,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(NG), 1)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
   }
+  // (the set-up above overlaps the previous kernel on the stream; global
+  // memory is touched only after it has completed)
+  grid_dep_wait();
+  if (threadIdx.x == 0) *abort_flag = (*(volatile int*)p.err != 0) ? 1 : 0;  // an earlier CTA failed: skip work
   tc_fence_before();
   cluster_sync_all();  // barriers of both CTAs initialised before any remote arrive
   tc_fence_after();
@@ -1099,7 +1105,9 @@ cudaError_t launch_tf32(const FwdParams& p, cudaStream_t s, int n_split = 1, flo
   const size_t rows = (size_t)p.bh * p.sq;
   float* split_lse = n_split > 1 ? ws + (size_t)n_split * rows * D : nullptr;
   dim3 grid(p.bh, n_qt, n_split);
-  tc_fwd_tf32<D, BK, VK, NKS, NVS><<<grid, kThreads, C::kSmemBytes, s>>>(mk, mv, p, ws, split_lse);
+  cudaError_t le = launch_pdl(tc_fwd_tf32<D, BK, VK, NKS, NVS>, grid, dim3(kThreads), C::kSmemBytes, s,
+                              mk, mv, p, ws, split_lse);
+  if (le != cudaSuccess) return le;
   count_launch();
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess || n_split == 1) return e;
@@ -1141,8 +1149,10 @@ cudaError_t launch_tf32_pair(const FwdParams& p, cudaStream_t s, int n_split = 1
   // persistent: one cluster (2 SMs) per SM pair, at most one per work tile
   const int n_clusters = (int)(n_work < sm_count[dev & 63] / 2 ? n_work : sm_count[dev & 63] / 2);
   if (n_work > INT32_MAX) return cudaErrorInvalidValue;
-  tc_fwd_tf32_pair<D, BK, NKS, NVS, NG><<<dim3(2 * n_clusters), pair_threads(NG), C::kSmemBytes, s>>>(
-      mk, mv, mq, mo, p, n_pairs, n_split, ws_lse);
+  cudaError_t le = launch_pdl(tc_fwd_tf32_pair<D, BK, NKS, NVS, NG>, dim3(2 * n_clusters),
+                              dim3(pair_threads(NG)), C::kSmemBytes, s, mk, mv, mq, mo, p, n_pairs,
+                              n_split, ws_lse);
+  if (le != cudaSuccess) return le;
   count_launch();
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess || n_split == 1) return e;

@@ -30,6 +30,7 @@ namespace {
 __global__ void __launch_bounds__(256) split_lo(const float4* __restrict__ k,
                                                 const float4* __restrict__ v,
                                                 float4* __restrict__ lo, size_t n4) {
+  grid_dep_wait();  // (launched with launch_pdl)
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < 2 * n4;
        i += (size_t)gridDim.x * blockDim.x) {
     const float4 x = i < n4 ? k[i] : v[i - n4];
@@ -131,7 +132,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(bar_o_done, 1);
     mbar_init(bar_drain, 1);
     mbar_init(bar_o_final, 1);
-    *abort_flag = (*(volatile int*)p.err != 0) ? 1 : 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   }
@@ -142,6 +142,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
+  // (the set-up above overlaps the previous kernel on the stream; global
+  // memory is touched only after it has completed)
+  grid_dep_wait();
+  if (threadIdx.x == 0) *abort_flag = (*(volatile int*)p.err != 0) ? 1 : 0;  // an earlier CTA failed: skip work
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -543,7 +547,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     mbar_init(bar_o_final, 1);
     mbar_init(bar_q_smem_full, 1);
     mbar_init(bar_q_smem_empty, 1);
-    *abort_flag = (*(volatile int*)p.err != 0) ? 1 : 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
@@ -553,6 +556,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
   }
+  // (the set-up above overlaps the previous kernel on the stream; global
+  // memory is touched only after it has completed)
+  grid_dep_wait();
+  if (threadIdx.x == 0) *abort_flag = (*(volatile int*)p.err != 0) ? 1 : 0;  // an earlier CTA failed: skip work
   tc_fence_before();
   cluster_sync_all();
   tc_fence_after();
@@ -937,9 +944,13 @@ cudaError_t launch_3x_pair(const FwdParams& p, float* ws, int n_split, int num_s
   const size_t n = (size_t)p.bh * p.sk * D;  // floats per K (or V) plane
   float* kl = ws;
   float* vl = ws + n;
-  split_lo<<<148 * 8, 256, 0, s>>>(reinterpret_cast<const float4*>(p.k),
-                                   reinterpret_cast<const float4*>(p.v),
-                                   reinterpret_cast<float4*>(ws), n / 4);
+  {
+    cudaError_t le = launch_pdl(split_lo, dim3(148 * 8), dim3(256), 0, s,
+                                reinterpret_cast<const float4*>(p.k),
+                                reinterpret_cast<const float4*>(p.v), reinterpret_cast<float4*>(ws),
+                                n / 4);
+    if (le != cudaSuccess) return le;
+  }
   count_launch(1);
   CUtensorMap mkh, mkl, mvh, mvl, mq;
   if (!make_map(&mkh, p.k, D, p.sk, p.bh, BK / 2, CU_TENSOR_MAP_SWIZZLE_128B) ||
@@ -966,8 +977,10 @@ cudaError_t launch_3x_pair(const FwdParams& p, float* ws, int n_split, int num_s
   const long long n_work = (long long)n_pairs * p.bh * n_split;
   if (n_work > INT32_MAX) return cudaErrorInvalidValue;
   const int n_clusters = (int)(n_work < num_sms / 2 ? n_work : num_sms / 2);
-  tc_fwd_3xtf32_pair<D, BK, NKS, NVS, NSB><<<dim3(2 * n_clusters), kThreads, C::kSmemBytes, s>>>(
-      mkh, mkl, mvh, mvl, mq, p, n_pairs, n_split, split_o, split_lse);
+  cudaError_t le = launch_pdl(tc_fwd_3xtf32_pair<D, BK, NKS, NVS, NSB>, dim3(2 * n_clusters),
+                              dim3(kThreads), C::kSmemBytes, s, mkh, mkl, mvh, mvl, mq, p, n_pairs,
+                              n_split, split_o, split_lse);
+  if (le != cudaSuccess) return le;
   count_launch();
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess || n_split == 1) return e;
@@ -980,9 +993,13 @@ cudaError_t launch_3x(const FwdParams& p, float* ws, int n_split, cudaStream_t s
   const size_t n = (size_t)p.bh * p.sk * D;  // floats per K (or V) plane
   float* kl = ws;
   float* vl = ws + n;
-  split_lo<<<148 * 8, 256, 0, s>>>(reinterpret_cast<const float4*>(p.k),
-                                   reinterpret_cast<const float4*>(p.v),
-                                   reinterpret_cast<float4*>(ws), n / 4);
+  {
+    cudaError_t le = launch_pdl(split_lo, dim3(148 * 8), dim3(256), 0, s,
+                                reinterpret_cast<const float4*>(p.k),
+                                reinterpret_cast<const float4*>(p.v), reinterpret_cast<float4*>(ws),
+                                n / 4);
+    if (le != cudaSuccess) return le;
+  }
   count_launch(1);
   CUtensorMap mkh, mkl, mvh, mvl;
   if (!make_map(&mkh, p.k, D, p.sk, p.bh, BK, CU_TENSOR_MAP_SWIZZLE_128B) ||
@@ -1007,8 +1024,9 @@ cudaError_t launch_3x(const FwdParams& p, float* ws, int n_split, cudaStream_t s
   const long long n_ctas = (long long)p.bh * ((p.sq + kBM - 1) / kBM);
   if (n_ctas > INT32_MAX) return cudaErrorInvalidValue;
   dim3 grid((unsigned)n_ctas, 1, n_split);
-  tc_fwd_3xtf32<D, BK, NKS, NVS, NSB><<<grid, kThreads, C::kSmemBytes, s>>>(mkh, mkl, mvh, mvl, p,
-                                                                            split_o, split_lse);
+  cudaError_t le = launch_pdl(tc_fwd_3xtf32<D, BK, NKS, NVS, NSB>, grid, dim3(kThreads), C::kSmemBytes,
+                              s, mkh, mkl, mvh, mvl, p, split_o, split_lse);
+  if (le != cudaSuccess) return le;
   count_launch();
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess || n_split == 1) return e;
