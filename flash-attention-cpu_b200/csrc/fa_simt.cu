@@ -26,6 +26,7 @@ constexpr int kSimtRows = 4;  // rows per warp
 
 template <int DCH>  // d <= 32 * DCH
 __global__ void __launch_bounds__(128) simt_fwd(FwdParams p) {
+  grid_dep_wait();  // (launched with launch_pdl)
   extern __shared__ float smem[];
   const int d = p.d;
   const int sk_stride = d | 1;  // odd row stride: lane-per-key reads are conflict-free
@@ -143,6 +144,7 @@ constexpr int kDecUnroll = 4;
 template <int NV>  // float4 slots per lane: d <= 128 * NV, d % 4 == 0
 __global__ void __launch_bounds__(256) decode_fwd(FwdParams p, int chunk, float* part_o,
                                                   float* part_lse) {
+  grid_dep_wait();  // (launched with launch_pdl)
   __shared__ float s_m[kDecWarps], s_l[kDecWarps];
   extern __shared__ float s_acc[];  // [kDecWarps][d]
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -374,9 +376,9 @@ cudaError_t launch_simt_t(const FwdParams& p, cudaStream_t s) {
     attr_set.fetch_or(bit);
   }
   dim3 grid((p.sq + kSimtBQ - 1) / kSimtBQ, p.bh);
-  simt_fwd<DCH><<<grid, 128, smem, s>>>(p);
+  cudaError_t le = launch_pdl(simt_fwd<DCH>, grid, dim3(128), smem, s, p);
   count_launch();
-  return cudaGetLastError();
+  return le != cudaSuccess ? le : cudaGetLastError();
 }
 
 }  // namespace
@@ -441,12 +443,11 @@ cudaError_t launch_decode(const FwdParams& p, int splits, float* scratch, cudaSt
   float* part_lse = scratch ? scratch + (size_t)splits * rows * p.d : nullptr;
   dim3 grid(p.sq, p.bh, splits);
   size_t smem = sizeof(float) * kDecWarps * p.d;
-  if (p.d <= 128)
-    decode_fwd<1><<<grid, 256, smem, s>>>(p, chunk, part_o, part_lse);
-  else
-    decode_fwd<2><<<grid, 256, smem, s>>>(p, chunk, part_o, part_lse);
+  cudaError_t e = p.d <= 128
+                      ? launch_pdl(decode_fwd<1>, grid, dim3(256), smem, s, p, chunk, part_o, part_lse)
+                      : launch_pdl(decode_fwd<2>, grid, dim3(256), smem, s, p, chunk, part_o, part_lse);
   count_launch();
-  cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess || splits == 1) return e;
   return launch_combine(part_o, part_lse, splits, (long long)rows, p.d, p.o, p.lse, s);
 }
