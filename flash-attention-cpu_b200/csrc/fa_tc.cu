@@ -95,6 +95,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 FwdParams p, float* split_o, float* split_lse) {
   using C = TcCfg<D, BK, VK, NKS, NVS>;
   constexpr int VS = C::kVS;
+  // (launched with launch_pdl: nothing below runs before the previous kernel on
+  // the stream has completed; a CTA's set-up takes ~0.2 us, so little is lost)
+  grid_dep_wait();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -156,6 +159,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(bar_o_done, 1);
     mbar_init(bar_drain, 1);
     mbar_init(bar_o_final, 1);
+    *abort_flag = (*(volatile int*)p.err != 0) ? 1 : 0;  // an earlier CTA failed: skip work
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   }
@@ -166,10 +170,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
-  // (the set-up above overlaps the previous kernel on the stream; global
-  // memory is touched only after it has completed)
-  grid_dep_wait();
-  if (threadIdx.x == 0) *abort_flag = (*(volatile int*)p.err != 0) ? 1 : 0;  // an earlier CTA failed: skip work
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -506,6 +506,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(NG), 1)
   // over them, and warp 3 stores that O by TMA and loads the next tile's Q
   // into the buffer.
   using C = PairCfg<D, BK, NKS, NVS, NG>;
+  // (launched with launch_pdl: nothing below runs before the previous kernel on
+  // the stream has completed; a CTA's set-up takes ~0.2 us, so little is lost)
+  grid_dep_wait();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -630,6 +633,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(NG), 1)
     mbar_init(bar_o_final, 1);
     mbar_init(bar_q_smem_full, 1);  // warp 3
     mbar_init(bar_o_smem_full, 4 * NG);  // the softmax warps of this CTA
+    *abort_flag = (*(volatile int*)p.err != 0) ? 1 : 0;  // an earlier CTA failed: skip work
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
@@ -639,10 +643,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads(NG), 1)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
   }
-  // (the set-up above overlaps the previous kernel on the stream; global
-  // memory is touched only after it has completed)
-  grid_dep_wait();
-  if (threadIdx.x == 0) *abort_flag = (*(volatile int*)p.err != 0) ? 1 : 0;  // an earlier CTA failed: skip work
   tc_fence_before();
   cluster_sync_all();  // barriers of both CTAs initialised before any remote arrive
   tc_fence_after();

@@ -70,6 +70,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                   const __grid_constant__ CUtensorMap tmVh, const __grid_constant__ CUtensorMap tmVl,
                   FwdParams p, float* split_o, float* split_lse) {
   using C = Tc3Cfg<D, BK, NKS, NVS, NSB>;
+  // (launched with launch_pdl: nothing below runs before the previous kernel on
+  // the stream has completed; a CTA's set-up takes ~0.2 us, so little is lost)
+  grid_dep_wait();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -132,6 +135,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(bar_o_done, 1);
     mbar_init(bar_drain, 1);
     mbar_init(bar_o_final, 1);
+    *abort_flag = (*(volatile int*)p.err != 0) ? 1 : 0;  // an earlier CTA failed: skip work
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   }
@@ -142,10 +146,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
-  // (the set-up above overlaps the previous kernel on the stream; global
-  // memory is touched only after it has completed)
-  grid_dep_wait();
-  if (threadIdx.x == 0) *abort_flag = (*(volatile int*)p.err != 0) ? 1 : 0;  // an earlier CTA failed: skip work
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -448,6 +448,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                        const __grid_constant__ CUtensorMap tmQ, FwdParams p, int n_pairs,
                        int n_split, float* split_o, float* split_lse) {
   using C = Tc3PairCfg<D, BK, NKS, NVS, NSB>;
+  // (launched with launch_pdl: nothing below runs before the previous kernel on
+  // the stream has completed; a CTA's set-up takes ~0.2 us, so little is lost)
+  grid_dep_wait();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -547,6 +550,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     mbar_init(bar_o_final, 1);
     mbar_init(bar_q_smem_full, 1);
     mbar_init(bar_q_smem_empty, 1);
+    *abort_flag = (*(volatile int*)p.err != 0) ? 1 : 0;  // an earlier CTA failed: skip work
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
@@ -556,10 +560,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
   }
-  // (the set-up above overlaps the previous kernel on the stream; global
-  // memory is touched only after it has completed)
-  grid_dep_wait();
-  if (threadIdx.x == 0) *abort_flag = (*(volatile int*)p.err != 0) ? 1 : 0;  // an earlier CTA failed: skip work
   tc_fence_before();
   cluster_sync_all();
   tc_fence_after();
