@@ -159,7 +159,7 @@ struct PinnedRing {
   bool busy[kSlots] = {};
   int next = 0;
 };
-// memcpy split over a fixed pool of host threads (single-threaded below 4 MB).
+// memcpy split over a fixed pool of host threads (single-threaded below 1 MB).
 void parallel_copy(void* dst, const void* src, size_t bytes);
 // true for memory the copy engines cannot read directly (not pinned or registered)
 bool is_pageable(const void* p);

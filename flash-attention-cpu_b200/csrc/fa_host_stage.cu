@@ -77,7 +77,7 @@ class CopyPool {
     for (auto& t : workers_) t.join();
   }
   void copy(char* dst, const char* src, size_t bytes) {
-    if (n_ == 1 || bytes < (size_t(4) << 20)) {
+    if (n_ == 1 || bytes < (size_t(1) << 20)) {  // (a hand-off costs ~10-50 us)
       copy_stream(dst, src, bytes);
       return;
     }
