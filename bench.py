@@ -378,8 +378,9 @@ def run_kv_split(args, cfg, rank, world, local, dev):
 def run_backward(args, cfg, q, k, v, out, lse, gen, rank, world, local, dev):
     """`--backward`: device time of fa_backward_device on the workload (forward
     output and LSE computed once beforehand).  FLOPs are the five matmuls of the
-    gradient (S, dP, dV, dQ, dK: 2.5x the forward's count); the kernels run on
-    the CUDA cores in f32 and recompute S and dP once more for dQ."""
+    gradient (S, dP, dV, dQ, dK: 2.5x the forward's count); both kernel families
+    recompute S and dP once more for dQ (seven matmuls executed).  At TF32
+    precision the tcgen05 kernels run; otherwise the exact f32 CUDA-core ones."""
     import torch
     import torch.distributed as dist
     import fa_b200
@@ -421,8 +422,12 @@ def run_backward(args, cfg, q, k, v, out, lse, gen, rank, world, local, dev):
         line = {"metric": "attention backward TFLOP/s", "value": fl / step_ms / 1e9,
                 "unit": "TFLOP/s", "n_gpus": world, "steps": steps, "warmup": args.warmup,
                 "ms_per_step": step_ms, "higher_is_better": True, "scaling": "strong",
-                "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-                "config": dict(config_dict(args, cfg, world), precision="f32 (CUDA cores)"),
+                "vs_baseline": None,
+                "dtype": "tf32" if fa_b200.last_path().startswith("tc_") else "f32",
+                "data": "synthetic",
+                "config": dict(config_dict(args, cfg, world),
+                               precision=("tf32 (tcgen05)" if fa_b200.last_path().startswith("tc_")
+                                          else "f32 (CUDA cores)")),
                 "clocks": clk.summary(wall0, wall1), "gpu_launches": launches,
                 "kernel": fa_b200.last_path()}
         print(json.dumps(line), flush=True)

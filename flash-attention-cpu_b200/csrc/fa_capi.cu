@@ -665,13 +665,23 @@ int fa_backward_device(const float* q, const float* k, const float* v, const flo
   p.bh = (int)bh; p.sq = (int)sq; p.sk = (int)sk; p.d = (int)d;
   p.causal = causal ? 1 : 0;
   p.scale = 1.0f / sqrtf((float)d);
+  p.err = g_dev[dev].err_flag;
+  p.wait_ns = g_wait_ns.load();
+  // TF32 precision on 16-byte aligned buffers with a supported head size runs
+  // the tensor-core kernels; everything else the exact f32 CUDA-core kernels.
+  bool aligned = true;
+  for (const void* ptr : {(const void*)q, (const void*)k, (const void*)v, (const void*)out,
+                          (const void*)dout, (const void*)dq, (const void*)dk, (const void*)dv})
+    aligned = aligned && (reinterpret_cast<uintptr_t>(ptr) & 15) == 0;
+  const bool tc = precision() == FA_PREC_TF32 && aligned && fa::tc_bwd_supported((int)d);
   float* ws = nullptr;
-  cudaError_t e = cudaMallocAsync((void**)&ws, fa::bwd_workspace_floats(p) * sizeof(float), s);
+  const size_t ws_floats = tc ? fa::tc_bwd_workspace_floats(p) : fa::bwd_workspace_floats(p);
+  cudaError_t e = cudaMallocAsync((void**)&ws, ws_floats * sizeof(float), s);
   if (e != cudaSuccess) return cuda_err(e, "cudaMallocAsync(backward workspace)");
-  e = fa::launch_bwd(p, ws, s);
+  e = tc ? fa::launch_tc_bwd(p, ws, s) : fa::launch_bwd(p, ws, s);
   cudaFreeAsync(ws, s);
   if (e != cudaSuccess) return cuda_err(e, "backward launch");
-  t_path = "simt_backward";
+  t_path = tc ? "tc_tf32_backward" : "simt_backward";
   return FA_OK;
 }
 

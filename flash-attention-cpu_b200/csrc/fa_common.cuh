@@ -46,6 +46,8 @@ struct BwdParams {
   long long q_offset, k_offset;
   int causal;
   float scale;
+  int* err;                    // device error word (the tensor-core kernels' bounded waits)
+  unsigned long long wait_ns;  // limit of those waits
 };
 
 enum ErrCode : int {
@@ -169,6 +171,11 @@ size_t bwd_workspace_floats(const BwdParams& p);
 // Enqueues the three backward kernels (d_head <= 128); `dvec` is workspace of
 // bwd_workspace_floats(p) floats.
 cudaError_t launch_bwd(BwdParams p, float* dvec, cudaStream_t s);
+// Tensor-core backward, TF32 (fa_bwd_tc.cu): d in {32, 64, 96, 128}, 16-byte
+// aligned buffers; `ws` is workspace of tc_bwd_workspace_floats(p) floats.
+bool tc_bwd_supported(int d);
+size_t tc_bwd_workspace_floats(const BwdParams& p);
+cudaError_t launch_tc_bwd(const BwdParams& p, float* ws, cudaStream_t s);
 cudaError_t staging_acquire(int dev, PinnedRing** in, PinnedRing** out, std::mutex** call);
 // One copy between host memory and device `dev` (current), enqueued on `s`.
 // Pageable host memory goes through the device's pinned rings with the copy

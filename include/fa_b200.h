@@ -184,9 +184,12 @@ FA_API int fa_forward_decode_noalloc(const float* q, const float* k, const float
 
 /* Gradients of the forward: given Q, K, V, the forward output O and its row
  * LSE (from fa_flash_attention_multihead_lse / fa_forward_device) and dO,
- * writes dQ [bh, seq_len_q, d_head], dK and dV [bh, seq_len_k, d_head].  Exact
- * f32 on the CUDA cores, any precision setting; d_head <= 128.  Same causal
- * convention as the forward (top-left).  Device buffers, async on `stream`. */
+ * writes dQ [bh, seq_len_q, d_head], dK and dV [bh, seq_len_k, d_head]; d_head
+ * <= 128.  At FA_PREC_TF32 with d_head in {32, 64, 96, 128} and 16-byte
+ * aligned buffers the tcgen05 kernels run (TF32 operands, f32 accumulation);
+ * otherwise exact f32 on the CUDA cores.  Same causal convention as the
+ * forward (top-left).  Device buffers, async on `stream`; a bounded-wait
+ * failure surfaces through fa_sync_status. */
 FA_API int fa_backward_device(const float* q, const float* k, const float* v, const float* out,
                               const float* lse, const float* dout, float* dq, float* dk,
                               float* dv, size_t batch_heads, size_t seq_len_q, size_t seq_len_k,

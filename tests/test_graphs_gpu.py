@@ -121,7 +121,8 @@ def test_many_calls_in_one_graph(fa):
         assert max_abs_diff(oo.cpu().numpy().ravel(), want) < TOL[0]
 
 
-def test_backward_replay_matches_eager(fa):
+@pytest.mark.parametrize("prec", [1, 0])  # CUDA-core and tensor-core backward
+def test_backward_replay_matches_eager(fa, prec):
     import torch
     bh, sq, sk, d = 2, 192, 256, 64
     q, k, v = _inputs(bh, sq, sk, d, 600)
@@ -132,7 +133,7 @@ def test_backward_replay_matches_eager(fa):
     o = torch.empty(bh, sq, d, device="cuda")
     lse = torch.empty(bh, sq, device="cuda")
     grads = [torch.empty_like(t) for t in (dq_in, dk_in, dv_in)]
-    fa.set_precision(1)
+    fa.set_precision(prec)
     side = torch.cuda.Stream()
     side.wait_stream(torch.cuda.current_stream())
     with torch.cuda.stream(side):
