@@ -42,7 +42,8 @@
 //   block's K (K-major), V (K-major), K (MN-major).  Per key block: S = Qs K^T,
 //   dP = dO V^T, dS written over S, then dQ += dS K.
 //
-// Warps: 0 TMA producer (one lane), 1 MMA issuer (one elected lane), 2..9
+// Warps: 0 and 10 TMA producers (one lane each: the operands of the scores,
+// then those of the gradient MMAs), 1 MMA issuer (one elected lane), 2..9
 // "softmax" warps: warp w reads TMEM lanes 32*(w%4).., and warps w and w+4
 // split each row's 64 columns.  All waits are bounded (kWaitLimitNs, or the
 // limit a test sets); on expiry the CTA raises its abort flag and the device
@@ -50,13 +51,16 @@
 // TMEM is freed.
 #include "fa_tc_ptx.cuh"
 
+#include <algorithm>
+
 namespace fa {
 namespace {
 
 constexpr int kTR = 128;      // rows of a CTA's own block (keys or query rows): MMA M
 constexpr int kTB = 64;       // rows per streamed block (queries or keys): MMA N
-constexpr int kTThreads = 320;
-constexpr int kTWarp0 = 2;    // first softmax warp
+constexpr int kTThreads = 352;
+constexpr int kTWarp0 = 2;     // softmax warps 2..9
+constexpr int kTWarpLate = 10;  // producer of the gradient MMAs' operands
 constexpr int kTSoftThreads = 256;
 constexpr float kLog2e = 1.44269504088896340736f;
 
@@ -72,7 +76,8 @@ struct BwdTcParams {
   long long q_offset, k_offset;
   int causal;
   float scale, scale_log2;
-  int n_kv_cta, n_q_cta;  // bh * ceil(sk/128) and bh * ceil(sq/128)
+  int nkb, nqb;       // key blocks (dK/dV CTAs) and query blocks (dQ CTAs) per slice
+  int group;          // slices per scheduling group
   int* err;
   unsigned long long wait_ns;
 };
@@ -91,27 +96,49 @@ struct BwdMaps {
   CUtensorMap vk;    // V, 64-key box, K-major         (dQ)
 };
 
+// Depth of each operand ring: every ring starts single, then rings are
+// doubled in the order given (earliest-needed operands first) while the
+// shared memory allows.
+constexpr int kSmemLimit = 232448 - 2048;  // room for barriers and alignment
+constexpr int ring_depth(int fixed, int tile, int n_rings, int which) {
+  int used = fixed + n_rings * tile;
+  for (int r = 0; r < n_rings; r++) {
+    if (used + tile > kSmemLimit) return 1;
+    used += tile;
+    if (r == which) return 2;
+  }
+  return 1;
+}
+
 template <int D>
 struct BwdTcCfg {
   static constexpr int kNsbKV = (3 * D + 4 * kTB <= 512) ? 2 : 1;
   static constexpr int kTileB = kTB * D * 4;   // one 64-row tile
   static constexpr int kTileA = kTR * D * 4;   // one 128-row tile
-  // dK/dV CTA: V | Q K-major | dO K-major | dO MN-major | Q MN-major | LSE2, D
-  static constexpr int kKvV = 0;
-  static constexpr int kKvQK = kTileA;
-  static constexpr int kKvOK = kKvQK + kTileB;
-  static constexpr int kKvOM = kKvOK + kTileB;
-  static constexpr int kKvQM = kKvOM + kTileB;
-  static constexpr int kKvVec = kKvQM + kTileB;
-  static constexpr int kEndKV = kKvVec + 2 * kTB * 4;
-  // dQ CTA: dO | K K-major | V K-major | K MN-major
-  static constexpr int kQDO = 0;
-  static constexpr int kQKK = kTileA;
-  static constexpr int kQVK = kQKK + kTileB;
-  static constexpr int kQKM = kQVK + kTileB;
-  static constexpr int kEndQ = kQKM + kTileB;
+  static constexpr int kVecBytes = 2 * kTB * 4;  // LSE2 and D of a 64-row block
+  // dK/dV CTA: V | rings Q K-major, dO K-major, dO MN-major, Q MN-major | LSE2, D
+  // (one per Q MN-major buffer)
+  static constexpr int kKvFixed = kTileA + 2 * kVecBytes;
+  static constexpr int kKvD0 = ring_depth(kKvFixed, kTileB, 4, 0);
+  static constexpr int kKvD1 = ring_depth(kKvFixed, kTileB, 4, 1);
+  static constexpr int kKvD2 = ring_depth(kKvFixed, kTileB, 4, 2);
+  static constexpr int kKvD3 = ring_depth(kKvFixed, kTileB, 4, 3);
+  static constexpr int kKvR0 = kTileA;
+  static constexpr int kKvR1 = kKvR0 + kKvD0 * kTileB;
+  static constexpr int kKvR2 = kKvR1 + kKvD1 * kTileB;
+  static constexpr int kKvR3 = kKvR2 + kKvD2 * kTileB;
+  static constexpr int kKvVec = kKvR3 + kKvD3 * kTileB;
+  static constexpr int kEndKV = kKvVec + 2 * kVecBytes;
+  // dQ CTA: dO | rings K K-major, V K-major, K MN-major
+  static constexpr int kQD0 = ring_depth(kTileA, kTileB, 3, 0);
+  static constexpr int kQD1 = ring_depth(kTileA, kTileB, 3, 1);
+  static constexpr int kQD2 = ring_depth(kTileA, kTileB, 3, 2);
+  static constexpr int kQR0 = kTileA;
+  static constexpr int kQR1 = kQR0 + kQD0 * kTileB;
+  static constexpr int kQR2 = kQR1 + kQD1 * kTileB;
+  static constexpr int kEndQ = kQR2 + kQD2 * kTileB;
   static constexpr int kOffBar = (kEndKV > kEndQ ? kEndKV : kEndQ);
-  static constexpr int kNumBars = 20;
+  static constexpr int kNumBars = 28;
   // At least 116 KB, so that two CTAs never share an SM: each allocates all
   // 512 TMEM columns, and a second one would wait for the first to finish.
   static constexpr int kSmemUsed = kOffBar + kNumBars * 8 + 16 + 1024;
@@ -140,18 +167,25 @@ __device__ __forceinline__ void mma_ss_elect(uint32_t d_tmem, uint64_t a_desc, u
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accum)
       : "memory");
 }
-// Descriptors of a [D/32][R][32] tile; `kk` selects the kk-th group of 8
-// elements along the inner product.  K-major (128-byte swizzle): the group
-// sits in chunk kk/4 at byte 32*(kk%4) of each row.  MN-major (32-byte-atom
-// swizzle): 8 rows = 1024 bytes per group, chunks R*128 bytes apart.
-template <int R>
-__device__ __forceinline__ uint64_t desc_k(uint32_t tile, int kk) {
-  return smem_desc(tile + (uint32_t)((kk >> 2) * R * 128 + (kk & 3) * 32), 16, 1024, kLayoutSw128);
+// Descriptors of a [D/32][R][32] tile, built once per tile; `kk` (a
+// compile-time loop index) selects the kk-th group of 8 elements along the
+// inner product, added to the start-address field (16-byte units).  K-major
+// (128-byte swizzle): the group sits in chunk kk/4 at byte 32*(kk%4) of each
+// row.  MN-major (32-byte-atom swizzle): 8 rows = 1024 bytes per group, chunks
+// R*128 bytes apart.
+__device__ __forceinline__ uint64_t desc_k_base(uint32_t tile) {
+  return smem_desc(tile, 16, 1024, kLayoutSw128);
 }
 template <int R>
-__device__ __forceinline__ uint64_t desc_mn(uint32_t tile, int kk) {
-  return smem_desc(tile + (uint32_t)kk * 1024u, R * 128, 512, kLayoutSw128Base32);
+__device__ __forceinline__ uint64_t desc_mn_base(uint32_t tile) {
+  return smem_desc(tile, R * 128, 512, kLayoutSw128Base32);
 }
+template <int R>
+constexpr uint64_t k_step(int kk) {
+  return (uint64_t)(((kk >> 2) * R * 128 + (kk & 3) * 32) >> 4);
+}
+constexpr uint64_t mn_step(int kk) { return (uint64_t)(kk * 64); }
+
 template <int D, int R>
 __device__ __forceinline__ void tma_tile(uint32_t dst, const CUtensorMap* map, uint32_t bar, int row,
                                          int bh) {
@@ -208,38 +242,63 @@ struct Bars {
   uint32_t b0;
   __device__ uint32_t operator()(int i) const { return b0 + 8u * (uint32_t)i; }
 };
-// Barrier indices.  Operand slots 0..3: dK/dV: Q K-major, dO K-major, dO
-// MN-major, Q MN-major (+ LSE2, D); dQ: K K-major, V K-major, K MN-major.
+// Barrier indices.
 constexpr int kBarStatic = 0;  // V (dK/dV) or dO (dQ) arrived
 constexpr int kBarStaged = 1;  // K (dK/dV) or Qs (dQ) staged in TMEM by the 256 softmax threads
-constexpr int kBarFull = 2;    // +slot: operand loaded
-constexpr int kBarEmpty = 6;   // +slot: operand slot free again
-constexpr int kBarS = 10;      // +buf: S (or S^T) complete
-constexpr int kBarDP = 12;     // +buf: dP (or dP^T) complete
-constexpr int kBarP = 14;      // +buf: P^T written (256 arrivals)
-constexpr int kBarDS = 16;     // +buf: dS written (256 arrivals)
-constexpr int kBarAcc = 18;    // the accumulators are final
-constexpr int kBarDrain = 19;  // every MMA issued has completed
+constexpr int kBarFull = 2;    // + 2 * ring + buffer: operand loaded
+constexpr int kBarEmpty = 10;  // + 2 * ring + buffer: buffer free again
+constexpr int kBarS = 18;      // +buf: S (or S^T) complete
+constexpr int kBarDP = 20;     // +buf: dP (or dP^T) complete
+constexpr int kBarP = 22;      // +buf: P^T written (256 arrivals)
+constexpr int kBarDS = 24;     // +buf: dS written (256 arrivals)
+constexpr int kBarAcc = 26;    // the accumulators are final
+constexpr int kBarDrain = 27;  // every MMA issued has completed
 
-// The producer's loads of one operand slot: block i waits until the MMA that
-// read block i-1 from the slot has completed.
-struct SlotLoader {
+// One operand stream: block i sits in buffer i % depth of the ring.  The
+// producer reuses a buffer once the MMA that read it last has completed (its
+// commit arrives on the buffer's empty barrier).
+struct Ring {
+  uint32_t base;
+  int bytes, depth, idx;
+  __device__ uint32_t buf(int i) const { return base + (uint32_t)((i % depth) * bytes); }
+  __device__ int full(int i) const { return kBarFull + 2 * idx + i % depth; }
+  __device__ int empty(int i) const { return kBarEmpty + 2 * idx + i % depth; }
+  __device__ uint32_t phase(int i) const { return (uint32_t)(i / depth) & 1u; }
+};
+struct Ctl {
   Bars bar;
   volatile int* abort_flag;
   int* err;
   unsigned long long wait_ns;
-  __device__ bool acquire(int slot, int i) const {
-    if (i == 0) return true;
-    return mbar_wait(bar(kBarEmpty + slot), (i - 1) & 1, abort_flag, err, wait_ns);
+  __device__ bool wait(int b, uint32_t parity) const {
+    return mbar_wait(bar(b), parity, abort_flag, err, wait_ns);
+  }
+  // producer: buffer of block i is free
+  __device__ bool acquire(const Ring& r, int i) const {
+    return i < r.depth || wait(r.empty(i), ((uint32_t)(i / r.depth) - 1u) & 1u);
+  }
+  // warp-wide (MMA warp): block i of the ring has landed
+  __device__ bool landed(const Ring& r, int i) const {
+    const bool w = wait(r.full(i), r.phase(i));
+    tc_fence_after();
+    return __all_sync(0xffffffffu, w);
+  }
+  // Bounded wait, ignoring the abort flag, for the last `n` loads' landing, so
+  // that no copy writes shared memory after the CTA exits.
+  __device__ void drain(const Ring& r, int n) const {
+    volatile int no_abort = 0;
+    for (int i = n > r.depth ? n - r.depth : 0; i < n; i++)
+      mbar_wait(bar(r.full(i)), r.phase(i), &no_abort, err);
   }
 };
 
 // ---------------------------------------------------------------- dK / dV CTA
 template <int D>
 __device__ void cta_dkdv(const BwdMaps& m, const BwdTcParams& p, int bh, int kb, uint32_t sbase,
-                         Bars bar, uint32_t tmem, volatile int* abort_flag) {
+                         const Ctl& ctl, uint32_t tmem) {
   using C = BwdTcCfg<D>;
   constexpr int NSB = C::kNsbKV;
+  const Bars bar = ctl.bar;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int k0 = kb * kTR;
   int q_first = 0;
@@ -249,101 +308,117 @@ __device__ void cta_dkdv(const BwdMaps& m, const BwdTcParams& p, int bh, int kb,
   }
   const int qb0 = q_first / kTB;
   const int nqb = (p.sq + kTB - 1) / kTB - qb0;
-  const uint32_t sV = sbase + C::kKvV, sQK = sbase + C::kKvQK, sOK = sbase + C::kKvOK;
-  const uint32_t sOM = sbase + C::kKvOM, sQM = sbase + C::kKvQM, sVec = sbase + C::kKvVec;
+  const uint32_t sV = sbase;
+  // rings: 0 Q K-major, 1 dO K-major, 2 dO MN-major, 3 Q MN-major (+ LSE2, D)
+  const Ring rQK{sbase + C::kKvR0, C::kTileB, C::kKvD0, 0};
+  const Ring rOK{sbase + C::kKvR1, C::kTileB, C::kKvD1, 1};
+  const Ring rOM{sbase + C::kKvR2, C::kTileB, C::kKvD2, 2};
+  const Ring rQM{sbase + C::kKvR3, C::kTileB, C::kKvD3, 3};
+  auto vec = [&](int i) { return sbase + C::kKvVec + (i % C::kKvD3) * C::kVecBytes; };
   const uint32_t t_k = tmem, t_dv = tmem + D, t_dk = tmem + 2 * D;
   auto t_s = [&](int b) { return tmem + 3 * D + b * 2 * kTB; };
   auto t_dp = [&](int b) { return tmem + 3 * D + b * 2 * kTB + kTB; };
-  const bool skip = *abort_flag != 0;
+  const bool skip = *ctl.abort_flag != 0;
 
-  if (warp == 0) {
+  if (warp == 0 || warp == kTWarpLate) {
+    // producers: warp 0 V and the operands the scores read (needed first),
+    // the late warp those of the gradient MMAs
     if (lane == 0 && !skip) {
-      mbar_expect_tx(bar(kBarStatic), C::kTileA);
-      tma_tile<D, kTR>(sV, &m.v128, bar(kBarStatic), k0, bh);
-      const SlotLoader sl{bar, abort_flag, p.err, p.wait_ns};
-      int loads[4] = {0, 0, 0, 0};  // loads issued per operand slot
-      for (int i = 0; i < nqb; i++) {
-        const int q0 = (qb0 + i) * kTB;
-        const size_t r0 = (size_t)bh * p.sq_pad + q0;
-        if (!sl.acquire(0, i)) break;
-        mbar_expect_tx(bar(kBarFull + 0), C::kTileB);
-        tma_tile<D, kTB>(sQK, &m.qk, bar(kBarFull + 0), q0, bh);
-        loads[0]++;
-        if (!sl.acquire(1, i)) break;
-        mbar_expect_tx(bar(kBarFull + 1), C::kTileB);
-        tma_tile<D, kTB>(sOK, &m.ok, bar(kBarFull + 1), q0, bh);
-        loads[1]++;
-        if (!sl.acquire(2, i)) break;
-        mbar_expect_tx(bar(kBarFull + 2), C::kTileB);
-        tma_tile<D, kTB>(sOM, &m.om, bar(kBarFull + 2), q0, bh);
-        loads[2]++;
-        if (!sl.acquire(3, i)) break;
-        mbar_expect_tx(bar(kBarFull + 3), C::kTileB + 2 * kTB * 4);
-        tma_tile<D, kTB>(sQM, &m.qm, bar(kBarFull + 3), q0, bh);
-        bulk_load(sVec, p.lse2 + r0, kTB * 4, bar(kBarFull + 3));
-        bulk_load(sVec + kTB * 4, p.dvec + r0, kTB * 4, bar(kBarFull + 3));
-        loads[3]++;
+      const bool early = warp == 0;
+      if (early) {
+        mbar_expect_tx(bar(kBarStatic), C::kTileA);
+        tma_tile<D, kTR>(sV, &m.v128, bar(kBarStatic), k0, bh);
       }
-      // Wait (bounded, ignoring the abort flag) for the last load of every
-      // slot, so no copy lands after the CTA exits even when a role aborted.
-      volatile int no_abort = 0;
-      mbar_wait(bar(kBarStatic), 0, &no_abort, p.err);
-      for (int sl_i = 0; sl_i < 4; sl_i++)
-        if (loads[sl_i] > 0) mbar_wait(bar(kBarFull + sl_i), (loads[sl_i] - 1) & 1, &no_abort, p.err);
+      // one producer's two rings, block by block (inlined per producer so the
+      // ring depths stay compile-time constants)
+      auto stream = [&](const Ring& ra, const CUtensorMap* ma, const Ring& rb,
+                        const CUtensorMap* mb, bool with_vec) {
+        int na = 0, nb = 0;
+        for (int i = 0; i < nqb; i++) {
+          const int q0 = (qb0 + i) * kTB;
+          if (!ctl.acquire(ra, i)) break;
+          mbar_expect_tx(bar(ra.full(i)), C::kTileB);
+          tma_tile<D, kTB>(ra.buf(i), ma, bar(ra.full(i)), q0, bh);
+          na++;
+          if (!ctl.acquire(rb, i)) break;
+          mbar_expect_tx(bar(rb.full(i)), C::kTileB + (with_vec ? C::kVecBytes : 0));
+          tma_tile<D, kTB>(rb.buf(i), mb, bar(rb.full(i)), q0, bh);
+          if (with_vec) {
+            const size_t r0 = (size_t)bh * p.sq_pad + q0;
+            bulk_load(vec(i), p.lse2 + r0, kTB * 4, bar(rb.full(i)));
+            bulk_load(vec(i) + kTB * 4, p.dvec + r0, kTB * 4, bar(rb.full(i)));
+          }
+          nb++;
+        }
+        ctl.drain(ra, na);
+        ctl.drain(rb, nb);
+      };
+      if (early) {
+        stream(rQK, &m.qk, rOK, &m.ok, false);
+        volatile int no_abort = 0;
+        mbar_wait(bar(kBarStatic), 0, &no_abort, p.err);
+      } else {
+        stream(rOM, &m.om, rQM, &m.qm, true);
+      }
     }
     __syncwarp();
   } else if (warp == 1) {
     if (!skip) {
       constexpr uint32_t idesc_s = instr_desc(kTR, kTB, false);
       constexpr uint32_t idesc_g = instr_desc(kTR, D, true);
-      bool ok = __all_sync(0xffffffffu, mbar_wait(bar(kBarStatic), 0, abort_flag, p.err, p.wait_ns));
-      ok = ok && __all_sync(0xffffffffu, mbar_wait(bar(kBarStaged), 0, abort_flag, p.err, p.wait_ns));
+      bool ok = __all_sync(0xffffffffu, ctl.wait(kBarStatic, 0));
+      ok = ok && __all_sync(0xffffffffu, ctl.wait(kBarStaged, 0));
       tc_fence_after();
-      auto wait_bar = [&](int b, int parity) {
-        const bool w = mbar_wait(bar(b), parity, abort_flag, p.err, p.wait_ns);
-        tc_fence_after();
-        return __all_sync(0xffffffffu, w);
-      };
-      auto issue_s = [&](int i) {  // S^T = K Qs^T
-        if (!wait_bar(kBarFull + 0, i & 1)) return false;
+      auto issue_s = [&](int i) {  // S^T = K Q^T
+        if (!ctl.landed(rQK, i)) return false;
         const int b = i % NSB;
+        const uint64_t bd = desc_k_base(rQK.buf(i));
+        const uint32_t ts = t_s(b);
 #pragma unroll
         for (int kk = 0; kk < D / 8; kk++)
-          mma_ts_elect(t_s(b), t_k + kk * 8, desc_k<kTB>(sQK, kk), idesc_s, kk > 0);
+          mma_ts_elect(ts, t_k + kk * 8, bd + k_step<kTB>(kk), idesc_s, kk > 0);
         tc_commit_elect(bar(kBarS + b));
-        tc_commit_elect(bar(kBarEmpty + 0));
+        tc_commit_elect(bar(rQK.empty(i)));
         return true;
       };
       auto issue_dp = [&](int i) {  // dP^T = V dO^T
-        if (!wait_bar(kBarFull + 1, i & 1)) return false;
+        if (!ctl.landed(rOK, i)) return false;
         const int b = i % NSB;
+        const uint64_t ad = desc_k_base(sV), bd = desc_k_base(rOK.buf(i));
+        const uint32_t td = t_dp(b);
 #pragma unroll
         for (int kk = 0; kk < D / 8; kk++)
-          mma_ss_elect(t_dp(b), desc_k<kTR>(sV, kk), desc_k<kTB>(sOK, kk), idesc_s, kk > 0);
+          mma_ss_elect(td, ad + k_step<kTR>(kk), bd + k_step<kTB>(kk), idesc_s, kk > 0);
         tc_commit_elect(bar(kBarDP + b));
-        tc_commit_elect(bar(kBarEmpty + 1));
+        tc_commit_elect(bar(rOK.empty(i)));
         return true;
       };
       auto issue_dv = [&](int i) {  // dV += P^T dO
         const int b = i % NSB;
-        if (!wait_bar(kBarFull + 2, i & 1)) return false;
-        if (!wait_bar(kBarP + b, (i / NSB) & 1)) return false;
+        if (!ctl.landed(rOM, i)) return false;
+        if (!__all_sync(0xffffffffu, ctl.wait(kBarP + b, (i / NSB) & 1))) return false;
+        tc_fence_after();
+        const uint64_t bd = desc_mn_base<kTB>(rOM.buf(i));
+        const uint32_t ta = t_s(b);
+        const uint32_t acc0 = i > 0 ? 1u : 0u;
 #pragma unroll
         for (int kk = 0; kk < kTB / 8; kk++)
-          mma_ts_elect(t_dv, t_s(b) + kk * 8, desc_mn<kTB>(sOM, kk), idesc_g,
-                       (i > 0 || kk > 0) ? 1u : 0u);
-        tc_commit_elect(bar(kBarEmpty + 2));
+          mma_ts_elect(t_dv, ta + kk * 8, bd + mn_step(kk), idesc_g, kk > 0 ? 1u : acc0);
+        tc_commit_elect(bar(rOM.empty(i)));
         return true;
       };
       auto issue_dk = [&](int i) {  // dK += dS^T Q
         const int b = i % NSB;
-        if (!wait_bar(kBarFull + 3, i & 1)) return false;
-        if (!wait_bar(kBarDS + b, (i / NSB) & 1)) return false;
+        if (!ctl.landed(rQM, i)) return false;
+        if (!__all_sync(0xffffffffu, ctl.wait(kBarDS + b, (i / NSB) & 1))) return false;
+        tc_fence_after();
+        const uint64_t bd = desc_mn_base<kTB>(rQM.buf(i));
+        const uint32_t ta = t_dp(b);
+        const uint32_t acc0 = i > 0 ? 1u : 0u;
 #pragma unroll
         for (int kk = 0; kk < kTB / 8; kk++)
-          mma_ts_elect(t_dk, t_dp(b) + kk * 8, desc_mn<kTB>(sQM, kk), idesc_g,
-                       (i > 0 || kk > 0) ? 1u : 0u);
-        tc_commit_elect(bar(kBarEmpty + 3));
+          mma_ts_elect(t_dk, ta + kk * 8, bd + mn_step(kk), idesc_g, kk > 0 ? 1u : acc0);
+        tc_commit_elect(bar(rQM.empty(i)));
         return true;
       };
       for (int i = 0; i < nqb && ok; i++) {
@@ -378,18 +453,17 @@ __device__ void cta_dkdv(const BwdMaps& m, const BwdTcParams& p, int bh, int kb,
       mbar_arrive(bar(kBarStaged));
     }
     const long long kg = p.k_offset + k0 + j;
-    const float* svec = reinterpret_cast<const float*>(__cvta_shared_to_generic(sVec));
     const float c = p.scale_log2;
     for (int i = 0; i < nqb && ok; i++) {
       const int b = i % NSB;
       const long long qg0 = p.q_offset + (long long)(qb0 + i) * kTB + 32 * h;
       // P of column e is nonzero only for e >= lo (causal)
       const long long lo = p.causal ? kg - qg0 : -1;
-      ok = __all_sync(0xffffffffu,
-                      mbar_wait(bar(kBarFull + 3), i & 1, abort_flag, p.err, p.wait_ns) &&
-                          mbar_wait(bar(kBarS + b), (i / NSB) & 1, abort_flag, p.err, p.wait_ns));
+      ok = __all_sync(0xffffffffu, ctl.wait(rQM.full(i), rQM.phase(i)) &&
+                                       ctl.wait(kBarS + b, (i / NSB) & 1));
       if (!ok) break;
       tc_fence_after();
+      const float* svec = reinterpret_cast<const float*>(__cvta_shared_to_generic(vec(i)));
       uint32_t x[32];
       tmem_ld32(t_s(b) + lane_off + 32 * h, x);
       tmem_wait_ld_regs(x);
@@ -412,8 +486,7 @@ __device__ void cta_dkdv(const BwdMaps& m, const BwdTcParams& p, int bh, int kb,
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(bar(kBarP + b));
-      ok = __all_sync(0xffffffffu,
-                      mbar_wait(bar(kBarDP + b), (i / NSB) & 1, abort_flag, p.err, p.wait_ns));
+      ok = __all_sync(0xffffffffu, ctl.wait(kBarDP + b, (i / NSB) & 1));
       if (!ok) break;
       tc_fence_after();
       tmem_ld32(t_dp(b) + lane_off + 32 * h, x);
@@ -432,7 +505,7 @@ __device__ void cta_dkdv(const BwdMaps& m, const BwdTcParams& p, int bh, int kb,
       mbar_arrive(bar(kBarDS + b));
     }
     if (nqb > 0) {
-      const bool w = ok ? mbar_wait(bar(kBarAcc), 0, abort_flag, p.err, p.wait_ns) : false;
+      const bool w = ok ? ctl.wait(kBarAcc, 0) : false;
       ok = __all_sync(0xffffffffu, w);
     }
     if (ok) {
@@ -454,85 +527,100 @@ __device__ void cta_dkdv(const BwdMaps& m, const BwdTcParams& p, int bh, int kb,
 // ---------------------------------------------------------------- dQ CTA
 template <int D>
 __device__ void cta_dq(const BwdMaps& m, const BwdTcParams& p, int bh, int qb, uint32_t sbase,
-                       Bars bar, uint32_t tmem, volatile int* abort_flag) {
+                       const Ctl& ctl, uint32_t tmem) {
   using C = BwdTcCfg<D>;
+  const Bars bar = ctl.bar;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int q0 = qb * kTR;
   const int q_rows = min(kTR, p.sq - q0);
   int kend = p.sk;
   if (p.causal) kend = causal_limit(p.q_offset + q0 + q_rows - 1, p.k_offset, p.sk);
   const int nkb = (kend + kTB - 1) / kTB;
-  const uint32_t sDO = sbase + C::kQDO, sKK = sbase + C::kQKK, sVK = sbase + C::kQVK;
-  const uint32_t sKM = sbase + C::kQKM;
+  const uint32_t sDO = sbase;
+  // rings: 0 K K-major, 1 V K-major, 2 K MN-major
+  const Ring rKK{sbase + C::kQR0, C::kTileB, C::kQD0, 0};
+  const Ring rVK{sbase + C::kQR1, C::kTileB, C::kQD1, 1};
+  const Ring rKM{sbase + C::kQR2, C::kTileB, C::kQD2, 2};
   const uint32_t t_q = tmem, t_dq = tmem + D;
   auto t_s = [&](int b) { return tmem + 2 * D + b * 2 * kTB; };
   auto t_dp = [&](int b) { return tmem + 2 * D + b * 2 * kTB + kTB; };
-  const bool skip = *abort_flag != 0;
+  const bool skip = *ctl.abort_flag != 0;
 
-  if (warp == 0) {
+  if (warp == 0 || warp == kTWarpLate) {
     if (lane == 0 && !skip) {
-      mbar_expect_tx(bar(kBarStatic), C::kTileA);
-      tma_tile<D, kTR>(sDO, &m.o128, bar(kBarStatic), q0, bh);
-      const SlotLoader sl{bar, abort_flag, p.err, p.wait_ns};
-      int loads[3] = {0, 0, 0};
-      for (int t = 0; t < nkb; t++) {
-        const int kr = t * kTB;
-        if (!sl.acquire(0, t)) break;
-        mbar_expect_tx(bar(kBarFull + 0), C::kTileB);
-        tma_tile<D, kTB>(sKK, &m.kk, bar(kBarFull + 0), kr, bh);
-        loads[0]++;
-        if (!sl.acquire(1, t)) break;
-        mbar_expect_tx(bar(kBarFull + 1), C::kTileB);
-        tma_tile<D, kTB>(sVK, &m.vk, bar(kBarFull + 1), kr, bh);
-        loads[1]++;
-        if (!sl.acquire(2, t)) break;
-        mbar_expect_tx(bar(kBarFull + 2), C::kTileB);
-        tma_tile<D, kTB>(sKM, &m.km, bar(kBarFull + 2), kr, bh);
-        loads[2]++;
+      const bool early = warp == 0;
+      int na = 0, nb = 0;
+      if (early) {
+        mbar_expect_tx(bar(kBarStatic), C::kTileA);
+        tma_tile<D, kTR>(sDO, &m.o128, bar(kBarStatic), q0, bh);
+        for (int t = 0; t < nkb; t++) {
+          if (!ctl.acquire(rKK, t)) break;
+          mbar_expect_tx(bar(rKK.full(t)), C::kTileB);
+          tma_tile<D, kTB>(rKK.buf(t), &m.kk, bar(rKK.full(t)), t * kTB, bh);
+          na++;
+          if (!ctl.acquire(rVK, t)) break;
+          mbar_expect_tx(bar(rVK.full(t)), C::kTileB);
+          tma_tile<D, kTB>(rVK.buf(t), &m.vk, bar(rVK.full(t)), t * kTB, bh);
+          nb++;
+        }
+        volatile int no_abort = 0;
+        mbar_wait(bar(kBarStatic), 0, &no_abort, p.err);
+        ctl.drain(rKK, na);
+        ctl.drain(rVK, nb);
+      } else {
+        for (int t = 0; t < nkb; t++) {
+          if (!ctl.acquire(rKM, t)) break;
+          mbar_expect_tx(bar(rKM.full(t)), C::kTileB);
+          tma_tile<D, kTB>(rKM.buf(t), &m.km, bar(rKM.full(t)), t * kTB, bh);
+          na++;
+        }
+        ctl.drain(rKM, na);
       }
-      volatile int no_abort = 0;
-      mbar_wait(bar(kBarStatic), 0, &no_abort, p.err);
-      for (int sl_i = 0; sl_i < 3; sl_i++)
-        if (loads[sl_i] > 0) mbar_wait(bar(kBarFull + sl_i), (loads[sl_i] - 1) & 1, &no_abort, p.err);
     }
     __syncwarp();
   } else if (warp == 1) {
     if (!skip) {
       constexpr uint32_t idesc_s = instr_desc(kTR, kTB, false);
       constexpr uint32_t idesc_g = instr_desc(kTR, D, true);
-      bool ok = __all_sync(0xffffffffu, mbar_wait(bar(kBarStatic), 0, abort_flag, p.err, p.wait_ns));
-      ok = ok && __all_sync(0xffffffffu, mbar_wait(bar(kBarStaged), 0, abort_flag, p.err, p.wait_ns));
+      bool ok = __all_sync(0xffffffffu, ctl.wait(kBarStatic, 0));
+      ok = ok && __all_sync(0xffffffffu, ctl.wait(kBarStaged, 0));
       tc_fence_after();
-      auto wait_bar = [&](int b, int parity) {
-        const bool w = mbar_wait(bar(b), parity, abort_flag, p.err, p.wait_ns);
-        tc_fence_after();
-        return __all_sync(0xffffffffu, w);
-      };
       auto issue_dq = [&](int t) {  // dQ += dS K
         const int b = t & 1;
-        if (!wait_bar(kBarFull + 2, t & 1)) return false;
-        if (!wait_bar(kBarDS + b, (t >> 1) & 1)) return false;
+        if (!ctl.landed(rKM, t)) return false;
+        if (!__all_sync(0xffffffffu, ctl.wait(kBarDS + b, (t >> 1) & 1))) return false;
+        tc_fence_after();
+        const uint64_t bd = desc_mn_base<kTB>(rKM.buf(t));
+        const uint32_t ta = t_s(b);
+        const uint32_t acc0 = t > 0 ? 1u : 0u;
 #pragma unroll
         for (int kk = 0; kk < kTB / 8; kk++)
-          mma_ts_elect(t_dq, t_s(b) + kk * 8, desc_mn<kTB>(sKM, kk), idesc_g,
-                       (t > 0 || kk > 0) ? 1u : 0u);
-        tc_commit_elect(bar(kBarEmpty + 2));
+          mma_ts_elect(t_dq, ta + kk * 8, bd + mn_step(kk), idesc_g, kk > 0 ? 1u : acc0);
+        tc_commit_elect(bar(rKM.empty(t)));
         return true;
       };
       for (int t = 0; t < nkb && ok; t++) {
         const int b = t & 1;
-        if (!(ok = wait_bar(kBarFull + 0, t & 1))) break;
+        if (!(ok = ctl.landed(rKK, t))) break;
+        {
+          const uint64_t bd = desc_k_base(rKK.buf(t));
+          const uint32_t ts = t_s(b);
 #pragma unroll
-        for (int kk = 0; kk < D / 8; kk++)  // S = Qs K^T
-          mma_ts_elect(t_s(b), t_q + kk * 8, desc_k<kTB>(sKK, kk), idesc_s, kk > 0);
+          for (int kk = 0; kk < D / 8; kk++)  // S = Qs K^T
+            mma_ts_elect(ts, t_q + kk * 8, bd + k_step<kTB>(kk), idesc_s, kk > 0);
+        }
         tc_commit_elect(bar(kBarS + b));
-        tc_commit_elect(bar(kBarEmpty + 0));
-        if (!(ok = wait_bar(kBarFull + 1, t & 1))) break;
+        tc_commit_elect(bar(rKK.empty(t)));
+        if (!(ok = ctl.landed(rVK, t))) break;
+        {
+          const uint64_t ad = desc_k_base(sDO), bd = desc_k_base(rVK.buf(t));
+          const uint32_t td = t_dp(b);
 #pragma unroll
-        for (int kk = 0; kk < D / 8; kk++)  // dP = dO V^T
-          mma_ss_elect(t_dp(b), desc_k<kTR>(sDO, kk), desc_k<kTB>(sVK, kk), idesc_s, kk > 0);
+          for (int kk = 0; kk < D / 8; kk++)  // dP = dO V^T
+            mma_ss_elect(td, ad + k_step<kTR>(kk), bd + k_step<kTB>(kk), idesc_s, kk > 0);
+        }
         tc_commit_elect(bar(kBarDP + b));
-        tc_commit_elect(bar(kBarEmpty + 1));
+        tc_commit_elect(bar(rVK.empty(t)));
         if (t > 0) ok = issue_dq(t - 1);
       }
       if (ok && nkb > 0 && issue_dq(nkb - 1)) tc_commit_elect(bar(kBarAcc));
@@ -565,8 +653,7 @@ __device__ void cta_dq(const BwdMaps& m, const BwdTcParams& p, int bh, int qb, u
       // visible columns [0, lim)
       int lim = min(32, p.sk - kc0);
       if (p.causal) lim = min(lim, causal_limit(qg, p.k_offset + kc0, 32));
-      ok = __all_sync(0xffffffffu,
-                      mbar_wait(bar(kBarS + b), (t >> 1) & 1, abort_flag, p.err, p.wait_ns));
+      ok = __all_sync(0xffffffffu, ctl.wait(kBarS + b, (t >> 1) & 1));
       if (!ok) break;
       tc_fence_after();
       uint32_t x[32];
@@ -579,8 +666,7 @@ __device__ void cta_dq(const BwdMaps& m, const BwdTcParams& p, int bh, int qb, u
 #pragma unroll
         for (int e = 0; e < 32; e++) pr[e] = (e < lim) ? pr[e] : 0.0f;
       }
-      ok = __all_sync(0xffffffffu,
-                      mbar_wait(bar(kBarDP + b), (t >> 1) & 1, abort_flag, p.err, p.wait_ns));
+      ok = __all_sync(0xffffffffu, ctl.wait(kBarDP + b, (t >> 1) & 1));
       if (!ok) break;
       tc_fence_after();
       tmem_ld32(t_dp(b) + lane_off + 32 * h, x);
@@ -593,7 +679,7 @@ __device__ void cta_dq(const BwdMaps& m, const BwdTcParams& p, int bh, int qb, u
       mbar_arrive(bar(kBarDS + b));
     }
     if (nkb > 0) {
-      const bool w = ok ? mbar_wait(bar(kBarAcc), 0, abort_flag, p.err, p.wait_ns) : false;
+      const bool w = ok ? ctl.wait(kBarAcc, 0) : false;
       ok = __all_sync(0xffffffffu, w);
     }
     if (ok) {
@@ -622,20 +708,27 @@ __global__ void __launch_bounds__(kTThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   const int warp = threadIdx.x >> 5;
 
-  // CTA i: the two kinds alternate while both last, heaviest causal blocks
+  // CTA order: slices in groups of p.group (a group's Q, K, V and dO fit in
+  // L2 together, so the CTAs of a slice find its tiles there); within a
+  // group, the two kinds alternate while both last, heaviest causal blocks
   // first (low key blocks for dK/dV, high query blocks for dQ).
-  const int i = blockIdx.x;
-  const int both = 2 * min(p.n_kv_cta, p.n_q_cta);
+  const int per_group = p.group * (p.nkb + p.nqb);
+  const int g = (int)blockIdx.x / per_group;
+  const int h0 = g * p.group;
+  const int gs = min(p.group, p.bh - h0);  // slices in this group
+  const int i = (int)blockIdx.x - g * per_group;
+  const int n_kv = gs * p.nkb, n_q = gs * p.nqb;
+  const int both = 2 * min(n_kv, n_q);
   bool is_kv;
   int rank;
   if (i < both) {
     is_kv = (i & 1) == 0;
     rank = i >> 1;
   } else {
-    is_kv = p.n_kv_cta > p.n_q_cta;
+    is_kv = n_kv > n_q;
     rank = i - both / 2;
   }
-  const int bh = rank % p.bh, blk = rank / p.bh;
+  const int bh = h0 + rank % gs, blk = rank / gs;
 
   if (threadIdx.x == 0) {
     for (int b = 0; b < C::kNumBars; b++) {
@@ -658,10 +751,11 @@ __global__ void __launch_bounds__(kTThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  const Ctl ctl{bar, abort_flag, p.err, p.wait_ns};
   if (is_kv)
-    cta_dkdv<D>(m, p, bh, blk, sbase, bar, tmem, abort_flag);
+    cta_dkdv<D>(m, p, bh, blk, sbase, ctl, tmem);
   else
-    cta_dq<D>(m, p, bh, (p.n_q_cta / p.bh) - 1 - blk, sbase, bar, tmem, abort_flag);
+    cta_dq<D>(m, p, bh, p.nqb - 1 - blk, sbase, ctl, tmem);
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
@@ -742,11 +836,14 @@ cudaError_t launch_tc_bwd_d(const BwdParams& bp, float* ws, cudaStream_t s) {
   p.q_offset = bp.q_offset; p.k_offset = bp.k_offset; p.causal = bp.causal;
   p.scale = bp.scale;
   p.scale_log2 = bp.scale * kLog2e;
-  p.n_kv_cta = bp.bh * ((bp.sk + kTR - 1) / kTR);
-  p.n_q_cta = bp.bh * (sq_pad / kTR);
+  p.nkb = (bp.sk + kTR - 1) / kTR;
+  p.nqb = sq_pad / kTR;
+  // Q, K, V and dO of `group` slices take at most ~48 MB (of the 126 MB L2).
+  const double slice_bytes = 4.0 * D * (2.0 * bp.sq + 2.0 * bp.sk);
+  p.group = (int)std::max(1.0, std::min((double)bp.bh, 48e6 / slice_bytes));
   p.err = bp.err;
   p.wait_ns = bp.wait_ns;
-  e = launch_pdl(tc_bwd_tf32<D>, dim3(p.n_kv_cta + p.n_q_cta), dim3(kTThreads),
+  e = launch_pdl(tc_bwd_tf32<D>, dim3(bp.bh * (p.nkb + p.nqb)), dim3(kTThreads),
                  (size_t)C::kSmemBytes, s, m, p);
   count_launch();
   return e;
