@@ -80,6 +80,7 @@ struct BwdTcParams {
   int group;          // slices per scheduling group
   int* err;
   unsigned long long wait_ns;
+  int test_skip;  // test hook: see the P arrive of the dK/dV CTA
 };
 
 // Tensor maps (3-D [bh][seq][d], boxes of 32 f32 x rows).  K-major maps use the
@@ -485,7 +486,8 @@ __device__ void cta_dkdv(const BwdMaps& m, const BwdTcParams& p, int bh, int kb,
       tmem_st32(t_s(b) + lane_off + 32 * h, x);
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(bar(kBarP + b));
+      // (test hook: one thread of the first CTA withholds its arrive)
+      if (!(p.test_skip == i && threadIdx.x == 64 && blockIdx.x == 0)) mbar_arrive(bar(kBarP + b));
       ok = __all_sync(0xffffffffu, ctl.wait(kBarDP + b, (i / NSB) & 1));
       if (!ok) break;
       tc_fence_after();
@@ -843,6 +845,7 @@ cudaError_t launch_tc_bwd_d(const BwdParams& bp, float* ws, cudaStream_t s) {
   p.group = (int)std::max(1.0, std::min((double)bp.bh, 48e6 / slice_bytes));
   p.err = bp.err;
   p.wait_ns = bp.wait_ns;
+  p.test_skip = bp.test_skip;
   e = launch_pdl(tc_bwd_tf32<D>, dim3(bp.bh * (p.nkb + p.nqb)), dim3(kTThreads),
                  (size_t)C::kSmemBytes, s, m, p);
   count_launch();

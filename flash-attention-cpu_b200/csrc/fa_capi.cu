@@ -667,6 +667,7 @@ int fa_backward_device(const float* q, const float* k, const float* v, const flo
   p.scale = 1.0f / sqrtf((float)d);
   p.err = g_dev[dev].err_flag;
   p.wait_ns = g_wait_ns.load();
+  p.test_skip = g_test_skip.load();
   // TF32 precision on 16-byte aligned buffers with a supported head size runs
   // the tensor-core kernels; everything else the exact f32 CUDA-core kernels.
   bool aligned = true;
@@ -735,7 +736,7 @@ int fa_flash_attention_backward(const float* q, const float* k, const float* v, 
   if (rc != FA_OK) return rc;
   if (e == cudaSuccess) e = e2;
   if (e != cudaSuccess) return cuda_err(e, "backward copies");
-  return FA_OK;
+  return check_err_flag(dev, s);  // a bounded wait that ran out (FA_ERR_TIMEOUT)
 }
 
 int fa_lse_combine_device(const float* o_parts, const float* lse_parts, size_t n_parts,

@@ -48,6 +48,7 @@ struct BwdParams {
   float scale;
   int* err;                    // device error word (the tensor-core kernels' bounded waits)
   unsigned long long wait_ns;  // limit of those waits
+  int test_skip;               // test hook, as FwdParams::test_skip (P of query block test_skip)
 };
 
 enum ErrCode : int {

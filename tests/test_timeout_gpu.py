@@ -73,3 +73,30 @@ def test_device_call_reports_the_timeout_through_sync_status(fa):
     want, _, _ = O.flash_v2_multihead(q.cpu().numpy().ravel(), k.cpu().numpy().ravel(),
                                       v.cpu().numpy().ravel(), bh, sq, sk, d, True)
     assert max_abs_diff(out.cpu().numpy().ravel(), want) < 2e-3
+
+
+@pytest.mark.parametrize("d", [64, 128])
+def test_backward_withheld_arrive_times_out_and_the_gpu_recovers(fa, d):
+    # The tensor-core backward: a softmax thread of the first dK/dV CTA
+    # withholds its "P ready" arrive on query block 0, the MMA issuer's wait
+    # for it runs out, and the host call reports FA_ERR_TIMEOUT; the next call
+    # gives the oracle's gradients.
+    bh, sq, sk = 2, 300, 400
+    q, k, v = random_vec(bh * sq * d, 31), random_vec(bh * sk * d, 32), random_vec(bh * sk * d, 33)
+    dout = random_vec(bh * sq * d, 34)
+    fa.set_precision(fa.PREC_FP32)
+    out, lse = fa.multihead_lse(q, k, v, bh, sq, sk, d, True)
+    fa.set_precision(fa.PREC_TF32)
+    fa.test_stall(0, 20_000_000)
+    try:
+        with pytest.raises(fa.FaError, match="FA_ERR_TIMEOUT"):
+            fa.flash_attention_backward(q, k, v, out, lse, dout, bh, sq, sk, d, True)
+    finally:
+        fa.test_stall(-1)
+    dq, dk, dv = fa.flash_attention_backward(q, k, v, out, lse, dout, bh, sq, sk, d, True)
+    assert fa.last_path() == "tc_tf32_backward"
+    for h in range(bh):
+        sl_q, sl_k = slice(h * sq * d, (h + 1) * sq * d), slice(h * sk * d, (h + 1) * sk * d)
+        rq, rk, rv = O.attention_backward_f64(q[sl_q], k[sl_k], v[sl_k], dout[sl_q], sq, sk, d, True)
+        for g, r in ((dq[sl_q], rq), (dk[sl_k], rk), (dv[sl_k], rv)):
+            assert np.max(np.abs(g - r)) < 2e-3 * (1.0 + np.max(np.abs(r)))
