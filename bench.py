@@ -683,6 +683,28 @@ def main():
                 "note": "attention TFLOP/s; the tensor pipe executes 3x these FLOPs "
                         "(hi*hi + hi*lo + lo*hi)",
                 "parity": p3}
+        # the backward pass (dQ, dK, dV; beyond the crate) on the same inputs,
+        # at TF32 (the tcgen05 kernels); its parity is in tests/test_backward.py
+        if args.precision == "tf32" and path.startswith("tcgen05") and d in (32, 64, 96, 128):
+            gen_b = np.random.default_rng(cfg[5] + 1000)
+            dout_b = torch.from_numpy(
+                gen_b.standard_normal(nh * sq * d, dtype=np.float32)).to(dev).view(nh, sq, d)
+            grads = [torch.empty_like(t) for t in (q, k, v)]
+
+            def bstep():
+                fa_b200.backward_device(q, k, v, out, lse, dout_b, *grads, causal=causal,
+                                        stream=stream)
+            for _ in range(3):
+                bstep()
+            steps_b = max(10, min(args.steps // 20, 200))
+            ms_b, l_b = time_device(fa_b200, bstep, steps_b, stream, world)
+            extra["backward"] = {
+                "value": 2.5 * fl_all / (ms_b * 1e-3) / 1e12, "unit": "TFLOP/s",
+                "ms_per_step": ms_b, "steps": steps_b, "kernel": fa_b200.last_path(),
+                "launches_per_step": l_b / steps_b,
+                "note": "gradient FLOPs (5 matmuls, 2.5x the forward); 7 executed",
+                "parity": "tests/test_backward.py (f64 oracle, 2e-3 relative at TF32)"}
+            del grads, dout_b
 
     # end-to-end through the crate API (host slices, synchronous): the call a
     # crate user makes, on this rank's slices; copies inside the timed region
