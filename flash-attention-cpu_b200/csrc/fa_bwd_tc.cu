@@ -117,8 +117,8 @@ struct BwdTcCfg {
   static constexpr int kTileB = kTB * D * 4;   // one 64-row tile
   static constexpr int kTileA = kTR * D * 4;   // one 128-row tile
   static constexpr int kVecBytes = 2 * kTB * 4;  // LSE2 and D of a 64-row block
-  // dK/dV CTA: V | rings Q K-major, dO K-major, dO MN-major, Q MN-major | LSE2, D
-  // (one per Q MN-major buffer)
+  // dK/dV CTA: V | rings Q K-major, dO K-major, dO MN-major, Q MN-major | two
+  // buffers of LSE2 and D
   static constexpr int kKvFixed = kTileA + 2 * kVecBytes;
   static constexpr int kKvD0 = ring_depth(kKvFixed, kTileB, 4, 0);
   static constexpr int kKvD1 = ring_depth(kKvFixed, kTileB, 4, 1);
@@ -139,7 +139,7 @@ struct BwdTcCfg {
   static constexpr int kQR2 = kQR1 + kQD1 * kTileB;
   static constexpr int kEndQ = kQR2 + kQD2 * kTileB;
   static constexpr int kOffBar = (kEndKV > kEndQ ? kEndKV : kEndQ);
-  static constexpr int kNumBars = 28;
+  static constexpr int kNumBars = 32;
   // At least 116 KB, so that two CTAs never share an SM: each allocates all
   // 512 TMEM columns, and a second one would wait for the first to finish.
   static constexpr int kSmemUsed = kOffBar + kNumBars * 8 + 16 + 1024;
@@ -254,6 +254,8 @@ constexpr int kBarP = 22;      // +buf: P^T written (256 arrivals)
 constexpr int kBarDS = 24;     // +buf: dS written (256 arrivals)
 constexpr int kBarAcc = 26;    // the accumulators are final
 constexpr int kBarDrain = 27;  // every MMA issued has completed
+constexpr int kBarVecFull = 28;   // +buf: LSE2 and D of a query block loaded (dK/dV CTA)
+constexpr int kBarVecEmpty = 30;  // +buf: the softmax warps are done with them (256 arrivals)
 
 // One operand stream: block i sits in buffer i % depth of the ring.  The
 // producer reuses a buffer once the MMA that read it last has completed (its
@@ -315,7 +317,13 @@ __device__ void cta_dkdv(const BwdMaps& m, const BwdTcParams& p, int bh, int kb,
   const Ring rOK{sbase + C::kKvR1, C::kTileB, C::kKvD1, 1};
   const Ring rOM{sbase + C::kKvR2, C::kTileB, C::kKvD2, 2};
   const Ring rQM{sbase + C::kKvR3, C::kTileB, C::kKvD3, 3};
-  auto vec = [&](int i) { return sbase + C::kKvVec + (i % C::kKvD3) * C::kVecBytes; };
+  // LSE2 and D of block i.  P needs LSE2 as soon as S^T is done.  With a
+  // double-buffered Q MN-major ring they ride with that tile (it lands early
+  // enough); with a single buffer (d = 96, 128) that tile waits for dK of the
+  // previous block, so they get their own two-deep ring, loaded after the
+  // scores' operands and released by the softmax warps after dS.
+  constexpr bool kVecRing = C::kKvD3 < 2;
+  auto vec = [&](int i) { return sbase + C::kKvVec + (i & 1) * C::kVecBytes; };
   const uint32_t t_k = tmem, t_dv = tmem + D, t_dk = tmem + 2 * D;
   auto t_s = [&](int b) { return tmem + 3 * D + b * 2 * kTB; };
   auto t_dp = [&](int b) { return tmem + 3 * D + b * 2 * kTB + kTB; };
@@ -333,8 +341,8 @@ __device__ void cta_dkdv(const BwdMaps& m, const BwdTcParams& p, int bh, int kb,
       // one producer's two rings, block by block (inlined per producer so the
       // ring depths stay compile-time constants)
       auto stream = [&](const Ring& ra, const CUtensorMap* ma, const Ring& rb,
-                        const CUtensorMap* mb, bool with_vec) {
-        int na = 0, nb = 0;
+                        const CUtensorMap* mb, bool first) {
+        int na = 0, nb = 0, nv = 0;
         for (int i = 0; i < nqb; i++) {
           const int q0 = (qb0 + i) * kTB;
           if (!ctl.acquire(ra, i)) break;
@@ -342,24 +350,36 @@ __device__ void cta_dkdv(const BwdMaps& m, const BwdTcParams& p, int bh, int kb,
           tma_tile<D, kTB>(ra.buf(i), ma, bar(ra.full(i)), q0, bh);
           na++;
           if (!ctl.acquire(rb, i)) break;
-          mbar_expect_tx(bar(rb.full(i)), C::kTileB + (with_vec ? C::kVecBytes : 0));
+          const bool vec_here = first == kVecRing;  // this producer loads LSE2 and D
+          mbar_expect_tx(bar(rb.full(i)), C::kTileB + (vec_here && !kVecRing ? C::kVecBytes : 0));
           tma_tile<D, kTB>(rb.buf(i), mb, bar(rb.full(i)), q0, bh);
-          if (with_vec) {
+          if (vec_here && !kVecRing) {
             const size_t r0 = (size_t)bh * p.sq_pad + q0;
             bulk_load(vec(i), p.lse2 + r0, kTB * 4, bar(rb.full(i)));
             bulk_load(vec(i) + kTB * 4, p.dvec + r0, kTB * 4, bar(rb.full(i)));
           }
           nb++;
+          if (vec_here && kVecRing) {
+            if (i >= 2 && !ctl.wait(kBarVecEmpty + (i & 1), (uint32_t)((i >> 1) - 1) & 1u)) break;
+            const size_t r0 = (size_t)bh * p.sq_pad + q0;
+            mbar_expect_tx(bar(kBarVecFull + (i & 1)), C::kVecBytes);
+            bulk_load(vec(i), p.lse2 + r0, kTB * 4, bar(kBarVecFull + (i & 1)));
+            bulk_load(vec(i) + kTB * 4, p.dvec + r0, kTB * 4, bar(kBarVecFull + (i & 1)));
+            nv++;
+          }
         }
         ctl.drain(ra, na);
         ctl.drain(rb, nb);
+        volatile int no_abort = 0;
+        for (int i = nv > 2 ? nv - 2 : 0; i < nv; i++)
+          mbar_wait(bar(kBarVecFull + (i & 1)), (uint32_t)(i >> 1) & 1u, &no_abort, p.err);
       };
       if (early) {
-        stream(rQK, &m.qk, rOK, &m.ok, false);
+        stream(rQK, &m.qk, rOK, &m.ok, true);
         volatile int no_abort = 0;
         mbar_wait(bar(kBarStatic), 0, &no_abort, p.err);
       } else {
-        stream(rOM, &m.om, rQM, &m.qm, true);
+        stream(rOM, &m.om, rQM, &m.qm, false);
       }
     }
     __syncwarp();
@@ -460,8 +480,9 @@ __device__ void cta_dkdv(const BwdMaps& m, const BwdTcParams& p, int bh, int kb,
       const long long qg0 = p.q_offset + (long long)(qb0 + i) * kTB + 32 * h;
       // P of column e is nonzero only for e >= lo (causal)
       const long long lo = p.causal ? kg - qg0 : -1;
-      ok = __all_sync(0xffffffffu, ctl.wait(rQM.full(i), rQM.phase(i)) &&
-                                       ctl.wait(kBarS + b, (i / NSB) & 1));
+      const bool vec_in = kVecRing ? ctl.wait(kBarVecFull + (i & 1), (uint32_t)(i >> 1) & 1u)
+                                   : ctl.wait(rQM.full(i), rQM.phase(i));
+      ok = __all_sync(0xffffffffu, vec_in && ctl.wait(kBarS + b, (i / NSB) & 1));
       if (!ok) break;
       tc_fence_after();
       const float* svec = reinterpret_cast<const float*>(__cvta_shared_to_generic(vec(i)));
@@ -502,6 +523,7 @@ __device__ void cta_dkdv(const BwdMaps& m, const BwdTcParams& p, int bh, int kb,
         x[e + 3] = __float_as_uint(pr[e + 3] * (__uint_as_float(x[e + 3]) - d4.w));
       }
       tmem_st32(t_dp(b) + lane_off + 32 * h, x);
+      if (kVecRing) mbar_arrive(bar(kBarVecEmpty + (i & 1)));  // LSE2 and D are read
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(bar(kBarDS + b));
@@ -734,7 +756,7 @@ __global__ void __launch_bounds__(kTThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int b = 0; b < C::kNumBars; b++) {
-      const bool many = b == kBarStaged || (b >= kBarP && b < kBarAcc);
+      const bool many = b == kBarStaged || (b >= kBarP && b < kBarAcc) || b >= kBarVecEmpty;
       mbar_init(bar(b), many ? kTSoftThreads : 1);
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
