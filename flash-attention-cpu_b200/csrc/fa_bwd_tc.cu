@@ -13,22 +13,25 @@
 // tile is loaded twice by TMA, once per layout (tensor maps with
 // CU_TENSOR_MAP_SWIZZLE_128B and CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B over the
 // same row-major tensor).  Every tile is [D/32 chunks][rows][32 f32].  Each
-// operand has its own single slot, freed by the commit of the MMA that reads it
-// last, so the next block's copy of an early operand (the scores' K-major
-// tiles) overlaps the current block's gradient MMAs.
+// operand streams through its own ring (one or two buffers, doubled in the
+// order the operands are needed while shared memory allows); a buffer is
+// freed by the commit of the MMA that reads it last, so the next block's copy
+// of an early operand (the scores' K-major tiles) overlaps the current
+// block's gradient MMAs.
 //
 // One launch runs two kinds of CTA (1 per SM: each allocates all 512 TMEM
-// columns), interleaved, heaviest causal blocks first.  A small prepass
-// writes LSE2 and D per query row (padded to a multiple of 128 rows: LSE2 =
-// +inf, D = 0 there, so padded rows get P = 0).
+// columns), interleaved, heaviest causal blocks first, slices in groups whose
+// tiles fit in L2 together.  A small prepass writes LSE2 and D per query row
+// (padded to a multiple of 128 rows: LSE2 = +inf, D = 0 there, so padded rows
+// get P = 0).
 //
 // dK/dV CTA: 128 keys of one slice (MMA M = 128, thread = key row).
 //   TMEM: K [0, D) (A operand of S^T, staged from registers), dV [D, 2D),
 //   dK [2D, 3D), then NSB buffers of S^T (64 cols) and dP^T (64 cols); NSB = 2
 //   when 3D + 256 <= 512, else 1.
-//   shared memory: V [128 keys] (K-major A of dP^T); slots for the 64-row
-//   query block's Q (K-major), dO (K-major), dO (MN-major), Q (MN-major) with
-//   that block's LSE2 and D.
+//   shared memory: V [128 keys] (K-major A of dP^T); rings for the 64-row
+//   query block's Q (K-major), dO (K-major), dO (MN-major), Q (MN-major), and
+//   two buffers for that block's LSE2 and D.
 //   Per 64-row query block: S^T = K Qs^T (A from TMEM, Q scaled in the
 //   softmax step), dP^T = V dO^T; the softmax warps overwrite S^T with P^T and
 //   dP^T with dS^T in place; then dV += P^T dO and dK += dS^T Q (A from TMEM,
@@ -38,7 +41,7 @@
 // dQ CTA: 128 query rows of one slice (thread = query row).
 //   TMEM: Qs [0, D) (scaled by c and rounded to TF32 while staged), dQ
 //   [D, 2D), two buffers of S (64) and dP (64).
-//   shared memory: dO [128 rows] (K-major A of dP); slots for the 64-key
+//   shared memory: dO [128 rows] (K-major A of dP); rings for the 64-key
 //   block's K (K-major), V (K-major), K (MN-major).  Per key block: S = Qs K^T,
 //   dP = dO V^T, dS written over S, then dQ += dS K.
 //
