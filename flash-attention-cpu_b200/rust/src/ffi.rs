@@ -66,6 +66,13 @@ extern "C" {
     pub fn fa_forward_device(q: *const f32, k: *const f32, v: *const f32, out: *mut f32,
         lse: *mut f32, batch_heads: usize, seq_len_q: usize, seq_len_k: usize, d_head: usize,
         causal: c_int, stream: *mut c_void) -> c_int;
+    pub fn fa_flash_attention_multihead_lse(q: *const f32, k: *const f32, v: *const f32,
+        batch_heads: usize, seq_len_q: usize, seq_len_k: usize, d_head: usize, causal: c_int,
+        out: *mut f32, lse: *mut f32) -> c_int;
+    pub fn fa_flash_attention_backward(q: *const f32, k: *const f32, v: *const f32,
+        out: *const f32, lse: *const f32, dout: *const f32, dq: *mut f32, dk: *mut f32,
+        dv: *mut f32, batch_heads: usize, seq_len_q: usize, seq_len_k: usize, d_head: usize,
+        causal: c_int) -> c_int;
     pub fn fa_sync_status(stream: *mut c_void) -> c_int;
     pub fn fa_set_precision(precision: c_int) -> c_int;
     pub fn fa_set_devices(devices: *const c_int, n: c_int) -> c_int;

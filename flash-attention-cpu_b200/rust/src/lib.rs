@@ -192,6 +192,57 @@ pub mod gpu {
         check(rc);
     }
 
+    /// The multihead forward on host slices that also returns the row LSE
+    /// (natural log of each row's scaled-score sum), as the backward needs it.
+    /// Panics on a shape mismatch, like the crate's entry points.
+    #[allow(clippy::too_many_arguments)]
+    pub fn flash_attention_multihead_lse(q: &[f32], k: &[f32], v: &[f32], batch: usize,
+                                         heads: usize, seq_len_q: usize, seq_len_k: usize,
+                                         d_head: usize, causal: bool) -> (Vec<f32>, Vec<f32>) {
+        let bh = batch * heads;
+        assert_eq!(q.len(), bh * seq_len_q * d_head, "q shape mismatch");
+        assert_eq!(k.len(), bh * seq_len_k * d_head, "k shape mismatch");
+        assert_eq!(v.len(), bh * seq_len_k * d_head, "v shape mismatch");
+        let mut out = vec![0.0f32; q.len()];
+        let mut lse = vec![0.0f32; bh * seq_len_q];
+        // SAFETY: every pointer covers the length checked above.
+        check(unsafe {
+            ffi::fa_flash_attention_multihead_lse(q.as_ptr(), k.as_ptr(), v.as_ptr(), bh,
+                                                  seq_len_q, seq_len_k, d_head, causal as i32,
+                                                  out.as_mut_ptr(), lse.as_mut_ptr())
+        });
+        (out, lse)
+    }
+
+    /// Gradients (dq, dk, dv) of the forward from its output `out`, row `lse`
+    /// and the output gradient `dout` (the crate itself is forward-only).  At
+    /// `Precision::Tf32` the tcgen05 kernels run (d_head 32, 64, 96, 128);
+    /// otherwise exact f32 on the CUDA cores.
+    #[allow(clippy::too_many_arguments)]
+    pub fn flash_attention_backward(q: &[f32], k: &[f32], v: &[f32], out: &[f32], lse: &[f32],
+                                    dout: &[f32], batch: usize, heads: usize, seq_len_q: usize,
+                                    seq_len_k: usize, d_head: usize, causal: bool)
+                                    -> (Vec<f32>, Vec<f32>, Vec<f32>) {
+        let bh = batch * heads;
+        let nq = bh * seq_len_q * d_head;
+        let nk = bh * seq_len_k * d_head;
+        assert_eq!(q.len(), nq, "q shape mismatch");
+        assert_eq!(k.len(), nk, "k shape mismatch");
+        assert_eq!(v.len(), nk, "v shape mismatch");
+        assert_eq!(out.len(), nq, "out shape mismatch");
+        assert_eq!(lse.len(), bh * seq_len_q, "lse shape mismatch");
+        assert_eq!(dout.len(), nq, "dout shape mismatch");
+        let (mut dq, mut dk, mut dv) = (vec![0.0f32; nq], vec![0.0f32; nk], vec![0.0f32; nk]);
+        // SAFETY: every pointer covers the length checked above.
+        check(unsafe {
+            ffi::fa_flash_attention_backward(q.as_ptr(), k.as_ptr(), v.as_ptr(), out.as_ptr(),
+                                             lse.as_ptr(), dout.as_ptr(), dq.as_mut_ptr(),
+                                             dk.as_mut_ptr(), dv.as_mut_ptr(), bh, seq_len_q,
+                                             seq_len_k, d_head, causal as i32)
+        });
+        (dq, dk, dv)
+    }
+
     /// Waits for `stream` and panics if a kernel of this library hit its
     /// bounded-wait limit (how the asynchronous device calls report failures).
     ///
