@@ -698,11 +698,17 @@ def main():
                 bstep()
             steps_b = max(10, min(args.steps // 20, 200))
             ms_b, l_b = time_device(fa_b200, bstep, steps_b, stream, world)
+            vb = 2.5 * fl_all / (ms_b * 1e-3) / 1e12
+            pk_b, pk_src_b = tensor_peak(measured_peaks(), ms_b * steps_b * 1e-3)
+            pk_b *= world
             extra["backward"] = {
-                "value": 2.5 * fl_all / (ms_b * 1e-3) / 1e12, "unit": "TFLOP/s",
+                "value": vb, "unit": "TFLOP/s",
                 "ms_per_step": ms_b, "steps": steps_b, "kernel": fa_b200.last_path(),
                 "launches_per_step": l_b / steps_b,
                 "note": "gradient FLOPs (5 matmuls, 2.5x the forward); 7 executed",
+                "roofline": {"bound": "tensor", "achieved": vb, "peak": pk_b, "unit": "TFLOP/s",
+                             "frac": vb / pk_b, "frac_executed": 1.4 * vb / pk_b,
+                             "peak_source": pk_src_b},
                 "parity": "tests/test_backward.py (f64 oracle, 2e-3 relative at TF32)"}
             del grads, dout_b
 
