@@ -25,14 +25,15 @@
 // (padded to a multiple of 128 rows: LSE2 = +inf, D = 0 there, so padded rows
 // get P = 0).
 //
-// dK/dV CTA: 128 keys of one slice (MMA M = 128, thread = key row).
+// dK/dV CTA: 128 keys of one slice (MMA M = 128, thread = key row), query
+//   blocks of QB rows: 128 at d <= 64, 64 above.
 //   TMEM: K [0, D) (A operand of S^T, staged from registers), dV [D, 2D),
-//   dK [2D, 3D), then NSB buffers of S^T (64 cols) and dP^T (64 cols); NSB = 2
-//   when 3D + 256 <= 512, else 1.
-//   shared memory: V [128 keys] (K-major A of dP^T); rings for the 64-row
-//   query block's Q (K-major), dO (K-major), dO (MN-major), Q (MN-major), and
-//   two buffers for that block's LSE2 and D.
-//   Per 64-row query block: S^T = K Qs^T (A from TMEM, Q scaled in the
+//   dK [2D, 3D), then NSB buffers of S^T (QB cols) and dP^T (QB cols); NSB = 2
+//   when they fit twice, else 1 (every supported d today).
+//   shared memory: V [128 keys] (K-major A of dP^T); rings for the query
+//   block's Q (K-major), dO (K-major), dO (MN-major), Q (MN-major), and two
+//   buffers for that block's LSE2 and D.
+//   Per query block: S^T = K Qs^T (A from TMEM, Q scaled in the
 //   softmax step), dP^T = V dO^T; the softmax warps overwrite S^T with P^T and
 //   dP^T with dS^T in place; then dV += P^T dO and dK += dS^T Q (A from TMEM,
 //   B MN-major).  With NSB = 1 the issue order dV_{i-1}, S^T_i, dK_{i-1},
@@ -116,22 +117,28 @@ constexpr int ring_depth(int fixed, int tile, int n_rings, int which) {
 
 template <int D>
 struct BwdTcCfg {
-  static constexpr int kNsbKV = (3 * D + 4 * kTB <= 512) ? 2 : 1;
-  static constexpr int kTileB = kTB * D * 4;   // one 64-row tile
+  // Query rows per block of the dK/dV CTA (the N of its score MMAs): 128 while
+  // TMEM holds K, dV, dK and one 128-column S^T / dP^T pair (d <= 64), so each
+  // block carries twice the MMA work per fixed cost (barrier checks, commits);
+  // else 64.
+  static constexpr int kQB = (3 * D + 4 * kTB <= 512) ? 2 * kTB : kTB;
+  static constexpr int kNsbKV = (3 * D + 4 * kQB <= 512) ? 2 : 1;
+  static constexpr int kTileB = kTB * D * 4;   // one 64-row tile (dQ CTA)
+  static constexpr int kTileQB = kQB * D * 4;  // one query-block tile (dK/dV CTA)
   static constexpr int kTileA = kTR * D * 4;   // one 128-row tile
-  static constexpr int kVecBytes = 2 * kTB * 4;  // LSE2 and D of a 64-row block
+  static constexpr int kVecBytes = 2 * kQB * 4;  // LSE2 and D of a query block
   // dK/dV CTA: V | rings Q K-major, dO K-major, dO MN-major, Q MN-major | two
   // buffers of LSE2 and D
   static constexpr int kKvFixed = kTileA + 2 * kVecBytes;
-  static constexpr int kKvD0 = ring_depth(kKvFixed, kTileB, 4, 0);
-  static constexpr int kKvD1 = ring_depth(kKvFixed, kTileB, 4, 1);
-  static constexpr int kKvD2 = ring_depth(kKvFixed, kTileB, 4, 2);
-  static constexpr int kKvD3 = ring_depth(kKvFixed, kTileB, 4, 3);
+  static constexpr int kKvD0 = ring_depth(kKvFixed, kTileQB, 4, 0);
+  static constexpr int kKvD1 = ring_depth(kKvFixed, kTileQB, 4, 1);
+  static constexpr int kKvD2 = ring_depth(kKvFixed, kTileQB, 4, 2);
+  static constexpr int kKvD3 = ring_depth(kKvFixed, kTileQB, 4, 3);
   static constexpr int kKvR0 = kTileA;
-  static constexpr int kKvR1 = kKvR0 + kKvD0 * kTileB;
-  static constexpr int kKvR2 = kKvR1 + kKvD1 * kTileB;
-  static constexpr int kKvR3 = kKvR2 + kKvD2 * kTileB;
-  static constexpr int kKvVec = kKvR3 + kKvD3 * kTileB;
+  static constexpr int kKvR1 = kKvR0 + kKvD0 * kTileQB;
+  static constexpr int kKvR2 = kKvR1 + kKvD1 * kTileQB;
+  static constexpr int kKvR3 = kKvR2 + kKvD2 * kTileQB;
+  static constexpr int kKvVec = kKvR3 + kKvD3 * kTileQB;
   static constexpr int kEndKV = kKvVec + 2 * kVecBytes;
   // dQ CTA: dO | rings K K-major, V K-major, K MN-major
   static constexpr int kQD0 = ring_depth(kTileA, kTileB, 3, 0);
@@ -149,7 +156,7 @@ struct BwdTcCfg {
   static constexpr int kSmemBytes = kSmemUsed > 118784 ? kSmemUsed : 118784;
   static_assert(D % 32 == 0 && D <= 128, "D in {32, 64, 96, 128}");
   static_assert(2 * D + 4 * kTB <= 512, "dQ TMEM budget");
-  static_assert(3 * D + 2 * kTB <= 512, "dK/dV TMEM budget");
+  static_assert(3 * D + 2 * kQB * kNsbKV <= 512, "dK/dV TMEM budget");
   static_assert(kSmemBytes <= 232448, "shared-memory budget");
 };
 
@@ -304,6 +311,8 @@ __device__ void cta_dkdv(const BwdMaps& m, const BwdTcParams& p, int bh, int kb,
                          const Ctl& ctl, uint32_t tmem) {
   using C = BwdTcCfg<D>;
   constexpr int NSB = C::kNsbKV;
+  constexpr int QB = C::kQB;          // query rows per block
+  constexpr int HALF = QB / 2;        // columns of a block per softmax thread
   const Bars bar = ctl.bar;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int k0 = kb * kTR;
@@ -312,14 +321,14 @@ __device__ void cta_dkdv(const BwdMaps& m, const BwdTcParams& p, int bh, int kb,
     const long long f = (long long)k0 + p.k_offset - p.q_offset;  // first row that sees key k0
     q_first = f <= 0 ? 0 : (f >= p.sq ? p.sq : (int)f);
   }
-  const int qb0 = q_first / kTB;
-  const int nqb = (p.sq + kTB - 1) / kTB - qb0;
+  const int qb0 = q_first / QB;
+  const int nqb = (p.sq + QB - 1) / QB - qb0;
   const uint32_t sV = sbase;
   // rings: 0 Q K-major, 1 dO K-major, 2 dO MN-major, 3 Q MN-major (+ LSE2, D)
-  const Ring rQK{sbase + C::kKvR0, C::kTileB, C::kKvD0, 0};
-  const Ring rOK{sbase + C::kKvR1, C::kTileB, C::kKvD1, 1};
-  const Ring rOM{sbase + C::kKvR2, C::kTileB, C::kKvD2, 2};
-  const Ring rQM{sbase + C::kKvR3, C::kTileB, C::kKvD3, 3};
+  const Ring rQK{sbase + C::kKvR0, C::kTileQB, C::kKvD0, 0};
+  const Ring rOK{sbase + C::kKvR1, C::kTileQB, C::kKvD1, 1};
+  const Ring rOM{sbase + C::kKvR2, C::kTileQB, C::kKvD2, 2};
+  const Ring rQM{sbase + C::kKvR3, C::kTileQB, C::kKvD3, 3};
   // LSE2 and D of block i.  P needs LSE2 as soon as S^T is done.  With a
   // double-buffered Q MN-major ring they ride with that tile (it lands early
   // enough); with a single buffer (d = 96, 128) that tile waits for dK of the
@@ -328,8 +337,8 @@ __device__ void cta_dkdv(const BwdMaps& m, const BwdTcParams& p, int bh, int kb,
   constexpr bool kVecRing = C::kKvD3 < 2;
   auto vec = [&](int i) { return sbase + C::kKvVec + (i & 1) * C::kVecBytes; };
   const uint32_t t_k = tmem, t_dv = tmem + D, t_dk = tmem + 2 * D;
-  auto t_s = [&](int b) { return tmem + 3 * D + b * 2 * kTB; };
-  auto t_dp = [&](int b) { return tmem + 3 * D + b * 2 * kTB + kTB; };
+  auto t_s = [&](int b) { return tmem + 3 * D + b * 2 * QB; };
+  auto t_dp = [&](int b) { return tmem + 3 * D + b * 2 * QB + QB; };
   const bool skip = *ctl.abort_flag != 0;
 
   if (warp == 0 || warp == kTWarpLate) {
@@ -347,27 +356,27 @@ __device__ void cta_dkdv(const BwdMaps& m, const BwdTcParams& p, int bh, int kb,
                         const CUtensorMap* mb, bool first) {
         int na = 0, nb = 0, nv = 0;
         for (int i = 0; i < nqb; i++) {
-          const int q0 = (qb0 + i) * kTB;
+          const int q0 = (qb0 + i) * QB;
           if (!ctl.acquire(ra, i)) break;
-          mbar_expect_tx(bar(ra.full(i)), C::kTileB);
-          tma_tile<D, kTB>(ra.buf(i), ma, bar(ra.full(i)), q0, bh);
+          mbar_expect_tx(bar(ra.full(i)), C::kTileQB);
+          tma_tile<D, QB>(ra.buf(i), ma, bar(ra.full(i)), q0, bh);
           na++;
           if (!ctl.acquire(rb, i)) break;
           const bool vec_here = first == kVecRing;  // this producer loads LSE2 and D
-          mbar_expect_tx(bar(rb.full(i)), C::kTileB + (vec_here && !kVecRing ? C::kVecBytes : 0));
-          tma_tile<D, kTB>(rb.buf(i), mb, bar(rb.full(i)), q0, bh);
+          mbar_expect_tx(bar(rb.full(i)), C::kTileQB + (vec_here && !kVecRing ? C::kVecBytes : 0));
+          tma_tile<D, QB>(rb.buf(i), mb, bar(rb.full(i)), q0, bh);
           if (vec_here && !kVecRing) {
             const size_t r0 = (size_t)bh * p.sq_pad + q0;
-            bulk_load(vec(i), p.lse2 + r0, kTB * 4, bar(rb.full(i)));
-            bulk_load(vec(i) + kTB * 4, p.dvec + r0, kTB * 4, bar(rb.full(i)));
+            bulk_load(vec(i), p.lse2 + r0, QB * 4, bar(rb.full(i)));
+            bulk_load(vec(i) + QB * 4, p.dvec + r0, QB * 4, bar(rb.full(i)));
           }
           nb++;
           if (vec_here && kVecRing) {
             if (i >= 2 && !ctl.wait(kBarVecEmpty + (i & 1), (uint32_t)((i >> 1) - 1) & 1u)) break;
             const size_t r0 = (size_t)bh * p.sq_pad + q0;
             mbar_expect_tx(bar(kBarVecFull + (i & 1)), C::kVecBytes);
-            bulk_load(vec(i), p.lse2 + r0, kTB * 4, bar(kBarVecFull + (i & 1)));
-            bulk_load(vec(i) + kTB * 4, p.dvec + r0, kTB * 4, bar(kBarVecFull + (i & 1)));
+            bulk_load(vec(i), p.lse2 + r0, QB * 4, bar(kBarVecFull + (i & 1)));
+            bulk_load(vec(i) + QB * 4, p.dvec + r0, QB * 4, bar(kBarVecFull + (i & 1)));
             nv++;
           }
         }
@@ -388,7 +397,7 @@ __device__ void cta_dkdv(const BwdMaps& m, const BwdTcParams& p, int bh, int kb,
     __syncwarp();
   } else if (warp == 1) {
     if (!skip) {
-      constexpr uint32_t idesc_s = instr_desc(kTR, kTB, false);
+      constexpr uint32_t idesc_s = instr_desc(kTR, QB, false);
       constexpr uint32_t idesc_g = instr_desc(kTR, D, true);
       bool ok = __all_sync(0xffffffffu, ctl.wait(kBarStatic, 0));
       ok = ok && __all_sync(0xffffffffu, ctl.wait(kBarStaged, 0));
@@ -400,7 +409,7 @@ __device__ void cta_dkdv(const BwdMaps& m, const BwdTcParams& p, int bh, int kb,
         const uint32_t ts = t_s(b);
 #pragma unroll
         for (int kk = 0; kk < D / 8; kk++)
-          mma_ts_elect(ts, t_k + kk * 8, bd + k_step<kTB>(kk), idesc_s, kk > 0);
+          mma_ts_elect(ts, t_k + kk * 8, bd + k_step<QB>(kk), idesc_s, kk > 0);
         tc_commit_elect(bar(kBarS + b));
         tc_commit_elect(bar(rQK.empty(i)));
         return true;
@@ -412,7 +421,7 @@ __device__ void cta_dkdv(const BwdMaps& m, const BwdTcParams& p, int bh, int kb,
         const uint32_t td = t_dp(b);
 #pragma unroll
         for (int kk = 0; kk < D / 8; kk++)
-          mma_ss_elect(td, ad + k_step<kTR>(kk), bd + k_step<kTB>(kk), idesc_s, kk > 0);
+          mma_ss_elect(td, ad + k_step<kTR>(kk), bd + k_step<QB>(kk), idesc_s, kk > 0);
         tc_commit_elect(bar(kBarDP + b));
         tc_commit_elect(bar(rOK.empty(i)));
         return true;
@@ -422,11 +431,11 @@ __device__ void cta_dkdv(const BwdMaps& m, const BwdTcParams& p, int bh, int kb,
         if (!ctl.landed(rOM, i)) return false;
         if (!__all_sync(0xffffffffu, ctl.wait(kBarP + b, (i / NSB) & 1))) return false;
         tc_fence_after();
-        const uint64_t bd = desc_mn_base<kTB>(rOM.buf(i));
+        const uint64_t bd = desc_mn_base<QB>(rOM.buf(i));
         const uint32_t ta = t_s(b);
         const uint32_t acc0 = i > 0 ? 1u : 0u;
 #pragma unroll
-        for (int kk = 0; kk < kTB / 8; kk++)
+        for (int kk = 0; kk < QB / 8; kk++)
           mma_ts_elect(t_dv, ta + kk * 8, bd + mn_step(kk), idesc_g, kk > 0 ? 1u : acc0);
         tc_commit_elect(bar(rOM.empty(i)));
         return true;
@@ -436,11 +445,11 @@ __device__ void cta_dkdv(const BwdMaps& m, const BwdTcParams& p, int bh, int kb,
         if (!ctl.landed(rQM, i)) return false;
         if (!__all_sync(0xffffffffu, ctl.wait(kBarDS + b, (i / NSB) & 1))) return false;
         tc_fence_after();
-        const uint64_t bd = desc_mn_base<kTB>(rQM.buf(i));
+        const uint64_t bd = desc_mn_base<QB>(rQM.buf(i));
         const uint32_t ta = t_dp(b);
         const uint32_t acc0 = i > 0 ? 1u : 0u;
 #pragma unroll
-        for (int kk = 0; kk < kTB / 8; kk++)
+        for (int kk = 0; kk < QB / 8; kk++)
           mma_ts_elect(t_dk, ta + kk * 8, bd + mn_step(kk), idesc_g, kk > 0 ? 1u : acc0);
         tc_commit_elect(bar(rQM.empty(i)));
         return true;
@@ -480,34 +489,37 @@ __device__ void cta_dkdv(const BwdMaps& m, const BwdTcParams& p, int bh, int kb,
     const float c = p.scale_log2;
     for (int i = 0; i < nqb && ok; i++) {
       const int b = i % NSB;
-      const long long qg0 = p.q_offset + (long long)(qb0 + i) * kTB + 32 * h;
-      // P of column e is nonzero only for e >= lo (causal)
-      const long long lo = p.causal ? kg - qg0 : -1;
       const bool vec_in = kVecRing ? ctl.wait(kBarVecFull + (i & 1), (uint32_t)(i >> 1) & 1u)
                                    : ctl.wait(rQM.full(i), rQM.phase(i));
       ok = __all_sync(0xffffffffu, vec_in && ctl.wait(kBarS + b, (i / NSB) & 1));
       if (!ok) break;
       tc_fence_after();
       const float* svec = reinterpret_cast<const float*>(__cvta_shared_to_generic(vec(i)));
-      uint32_t x[32];
-      tmem_ld32(t_s(b) + lane_off + 32 * h, x);
-      tmem_wait_ld_regs(x);
-      float pr[32];
+      float pr[HALF];
 #pragma unroll
-      for (int e = 0; e < 32; e += 4) {
-        const float4 l4 = *reinterpret_cast<const float4*>(svec + 32 * h + e);
-        pr[e] = ex2(fmaf(__uint_as_float(x[e]), c, -l4.x));
-        pr[e + 1] = ex2(fmaf(__uint_as_float(x[e + 1]), c, -l4.y));
-        pr[e + 2] = ex2(fmaf(__uint_as_float(x[e + 2]), c, -l4.z));
-        pr[e + 3] = ex2(fmaf(__uint_as_float(x[e + 3]), c, -l4.w));
+      for (int cc = 0; cc < HALF / 32; cc++) {  // 32 columns at a time
+        const int col = HALF * h + 32 * cc;
+        // P of column e is nonzero only for e >= lo (causal)
+        const long long lo = p.causal ? kg - (p.q_offset + (long long)(qb0 + i) * QB + col) : -1;
+        uint32_t x[32];
+        tmem_ld32(t_s(b) + lane_off + col, x);
+        tmem_wait_ld_regs(x);
+#pragma unroll
+        for (int e = 0; e < 32; e += 4) {
+          const float4 l4 = *reinterpret_cast<const float4*>(svec + col + e);
+          pr[32 * cc + e] = ex2(fmaf(__uint_as_float(x[e]), c, -l4.x));
+          pr[32 * cc + e + 1] = ex2(fmaf(__uint_as_float(x[e + 1]), c, -l4.y));
+          pr[32 * cc + e + 2] = ex2(fmaf(__uint_as_float(x[e + 2]), c, -l4.z));
+          pr[32 * cc + e + 3] = ex2(fmaf(__uint_as_float(x[e + 3]), c, -l4.w));
+        }
+        if (__any_sync(0xffffffffu, lo > 0)) {
+#pragma unroll
+          for (int e = 0; e < 32; e++) pr[32 * cc + e] = (e >= lo) ? pr[32 * cc + e] : 0.0f;
+        }
+#pragma unroll
+        for (int e = 0; e < 32; e++) x[e] = __float_as_uint(pr[32 * cc + e]);
+        tmem_st32(t_s(b) + lane_off + col, x);
       }
-      if (__any_sync(0xffffffffu, lo > 0)) {
-#pragma unroll
-        for (int e = 0; e < 32; e++) pr[e] = (e >= lo) ? pr[e] : 0.0f;
-      }
-#pragma unroll
-      for (int e = 0; e < 32; e++) x[e] = __float_as_uint(pr[e]);
-      tmem_st32(t_s(b) + lane_off + 32 * h, x);
       tmem_wait_st();
       tc_fence_before();
       // (test hook: one thread of the first CTA withholds its arrive)
@@ -515,17 +527,22 @@ __device__ void cta_dkdv(const BwdMaps& m, const BwdTcParams& p, int bh, int kb,
       ok = __all_sync(0xffffffffu, ctl.wait(kBarDP + b, (i / NSB) & 1));
       if (!ok) break;
       tc_fence_after();
-      tmem_ld32(t_dp(b) + lane_off + 32 * h, x);
-      tmem_wait_ld_regs(x);
 #pragma unroll
-      for (int e = 0; e < 32; e += 4) {
-        const float4 d4 = *reinterpret_cast<const float4*>(svec + kTB + 32 * h + e);
-        x[e] = __float_as_uint(pr[e] * (__uint_as_float(x[e]) - d4.x));
-        x[e + 1] = __float_as_uint(pr[e + 1] * (__uint_as_float(x[e + 1]) - d4.y));
-        x[e + 2] = __float_as_uint(pr[e + 2] * (__uint_as_float(x[e + 2]) - d4.z));
-        x[e + 3] = __float_as_uint(pr[e + 3] * (__uint_as_float(x[e + 3]) - d4.w));
+      for (int cc = 0; cc < HALF / 32; cc++) {
+        const int col = HALF * h + 32 * cc;
+        uint32_t x[32];
+        tmem_ld32(t_dp(b) + lane_off + col, x);
+        tmem_wait_ld_regs(x);
+#pragma unroll
+        for (int e = 0; e < 32; e += 4) {
+          const float4 d4 = *reinterpret_cast<const float4*>(svec + QB + col + e);
+          x[e] = __float_as_uint(pr[32 * cc + e] * (__uint_as_float(x[e]) - d4.x));
+          x[e + 1] = __float_as_uint(pr[32 * cc + e + 1] * (__uint_as_float(x[e + 1]) - d4.y));
+          x[e + 2] = __float_as_uint(pr[32 * cc + e + 2] * (__uint_as_float(x[e + 2]) - d4.z));
+          x[e + 3] = __float_as_uint(pr[32 * cc + e + 3] * (__uint_as_float(x[e + 3]) - d4.w));
+        }
+        tmem_st32(t_dp(b) + lane_off + col, x);
       }
-      tmem_st32(t_dp(b) + lane_off + 32 * h, x);
       if (kVecRing) mbar_arrive(bar(kBarVecEmpty + (i & 1)));  // LSE2 and D are read
       tmem_wait_st();
       tc_fence_before();
@@ -838,10 +855,10 @@ cudaError_t launch_tc_bwd_d(const BwdParams& bp, float* ws, cudaStream_t s) {
   BwdMaps m;
   const auto sw = CU_TENSOR_MAP_SWIZZLE_128B, sw32 = CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
   if (!make_map(&m.v128, bp.v, D, bp.sk, bp.bh, kTR, sw) ||
-      !make_map(&m.qk, bp.q, D, bp.sq, bp.bh, kTB, sw) ||
-      !make_map(&m.qm, bp.q, D, bp.sq, bp.bh, kTB, sw32) ||
-      !make_map(&m.ok, bp.dout, D, bp.sq, bp.bh, kTB, sw) ||
-      !make_map(&m.om, bp.dout, D, bp.sq, bp.bh, kTB, sw32) ||
+      !make_map(&m.qk, bp.q, D, bp.sq, bp.bh, C::kQB, sw) ||
+      !make_map(&m.qm, bp.q, D, bp.sq, bp.bh, C::kQB, sw32) ||
+      !make_map(&m.ok, bp.dout, D, bp.sq, bp.bh, C::kQB, sw) ||
+      !make_map(&m.om, bp.dout, D, bp.sq, bp.bh, C::kQB, sw32) ||
       !make_map(&m.o128, bp.dout, D, bp.sq, bp.bh, kTR, sw) ||
       !make_map(&m.kk, bp.k, D, bp.sk, bp.bh, kTB, sw) ||
       !make_map(&m.km, bp.k, D, bp.sk, bp.bh, kTB, sw32) ||
